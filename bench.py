@@ -1,0 +1,331 @@
+"""Benchmark: embedding tokens/s of the GPU-worker forward pass on B200.
+
+Workload (default, ``--workload c2``): Qwen3-Embedding-0.6B architecture, AWQ int4 weights
+(group 128, seeded synthetic), one packed varlen batch of 20 sequences x 1000 tokens,
+tensor parallel over ``--gpus`` ranks (TP=1 by default).  A step is one forward pass over
+the batch: embedding -> 28 decoder layers -> final norm (``value``), plus last-token
+pooling + L2 normalisation and the host copies for ``e2e``.
+
+* ``value``: tokens/s with the batch resident in HBM, device time from CUDA events,
+  barrier + synchronize around the K timed steps, max over ranks.
+* ``e2e``: the same batch through ``GPUWorker.embed`` (the reference's ``_inference`` +
+  post-process): pinned host ids/positions copied in, fp32 embeddings copied out, every
+  step.
+* ``roofline``: the AWQ GEMM (the dominant kernel), FLOPs of every launch in the timed
+  region / CUDA-event time of those launches, against the measured dense bf16 peak.
+* ``cpu_baseline``: the CPU oracle's fp32 forward (a restatement of the reference's torch
+  forward) on a bounded sample of the same workload, on the host's cores.
+
+``--impl reference`` times that CPU forward alone (rank 0; other ranks exit) and prints
+the same metric.  Run multi-GPU as
+``python -m torch.distributed.run --nproc-per-node N bench.py --gpus N``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "embedding tokens/sec (20x1000-tok batch)"
+UNIT = "tokens/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["mes", "reference"], default="mes")
+    ap.add_argument("--workload", choices=["c2", "c4", "c5"], default="c2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def workload(name: str):
+    from mes_b200 import synthetic
+    if name == "c2":
+        cfg = synthetic.qwen3_0_6b()
+        lengths = [1000] * 20
+        desc = "Qwen3-Embedding-0.6B arch, AWQ int4 g128, 20 x 1000 tokens"
+    elif name == "c4":
+        cfg = synthetic.qwen3_8b()
+        lengths = synthetic.lengths_log_uniform(120000, 64, 4096, seed=1)
+        desc = "Qwen3-Embedding-8B arch, AWQ int4 g128, 120000 tokens, log-uniform [64, 4096]"
+    else:
+        cfg = synthetic.qwen2_1_5b()
+        lengths = synthetic.lengths_uniform(64, 16, 512, seed=1)
+        desc = "Qwen2-1.5B arch, AWQ int4 g128, 64 seqs uniform [16, 512]"
+    return cfg, lengths, desc
+
+
+# ---------------------------------------------------------------------------- helpers
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), d["hbm_gbs"], "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_forward_tokens_per_s(cfg, sample_tokens: int, layers: int, threads: int,
+                             repeats: int = 1):
+    """The oracle's fp32 forward (dense weights of the same shapes) on `sample_tokens`
+    tokens through `layers` layers; returns tokens/s scaled to the full depth."""
+    import torch
+    from mes_b200 import synthetic
+    from oracle import model as omodel
+    torch.set_num_threads(threads)
+    w = synthetic.dense_weights(cfg, seed=0, num_layers=layers)
+    ids, pos, _ = synthetic.packed_batch([sample_tokens], cfg.vocab_size, seed=1)
+    ids, pos = torch.from_numpy(ids), torch.from_numpy(pos)
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        omodel.forward(cfg, w, ids, pos, qk_norm=not synthetic.is_qwen2(cfg), num_layers=layers)
+        times.append(time.perf_counter() - t0)
+    per_step = statistics.median(times) * cfg.num_hidden_layers / layers
+    return sample_tokens / per_step, per_step
+
+
+# ---------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg, lengths, desc = workload(args.workload)
+    threads = os.cpu_count() or 1
+    # Bounded per-step sample: one 1000-token sequence through a subset of the layers,
+    # scaled to the full depth, so that warmup + steps finish in a few minutes.
+    steps = max(args.steps, 1)
+    layers = max(1, min(cfg.num_hidden_layers, int(28 * 8 / (steps + args.warmup))))
+    import torch
+    from mes_b200 import synthetic
+    from oracle import model as omodel
+    torch.set_num_threads(threads)
+    w = synthetic.dense_weights(cfg, seed=0, num_layers=layers)
+    ids, pos, _ = synthetic.packed_batch([1000], cfg.vocab_size, seed=1)
+    ids, pos = torch.from_numpy(ids), torch.from_numpy(pos)
+    qk = not synthetic.is_qwen2(cfg)
+    for _ in range(args.warmup):
+        omodel.forward(cfg, w, ids, pos, qk_norm=qk, num_layers=layers)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        omodel.forward(cfg, w, ids, pos, qk_norm=qk, num_layers=layers)
+    dt = (time.perf_counter() - t0) / steps * cfg.num_hidden_layers / layers
+    value = 1000 / dt
+    sample = (f"1 x 1000 tokens through {layers} of {cfg.num_hidden_layers} layers per step, "
+              f"fp32, time scaled to full depth")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1000 * sum(lengths) / 1000, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": desc, "tokens": sum(lengths), "sequences": len(lengths)},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ---------------------------------------------------------------------------- GPU arm
+def run_mes(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__
+    __graft_entry__.build()
+    from mes_b200 import _C, synthetic
+    from mes_b200.core.gpu_worker import GPUWorker
+    from mes_b200.schemas.config import MESConfig
+    from mes_b200.ultils.loader import load_weights
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+
+    cfg, lengths, desc = workload(args.workload)
+    ids, pos, last = synthetic.packed_batch(lengths, cfg.vocab_size, seed=1)
+    T = len(ids)
+
+    worker = GPUWorker(MESConfig(model_config=cfg), device=dev)
+    # Seeded synthetic weights generated on the device (same seed on every rank; each
+    # rank's loaders keep only its shard).
+    weights = synthetic.awq_weights(cfg, seed=0, device=dev)
+    load_weights(worker.model, weights)
+    del weights
+    torch.cuda.empty_cache()
+
+    ids_d = torch.from_numpy(ids).to(dev)
+    pos_d = torch.from_numpy(pos).to(dev)
+    model = worker.model
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            model(ids_d, pos_d)
+        barrier()
+
+        # ---- device-resident timed region (value) -----------------------------------
+        _C.gemm_events = []
+        launches0 = _C.launch_count
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clocks:
+            barrier()
+            ev0.record()
+            for _ in range(args.steps):
+                model(ids_d, pos_d)
+            ev1.record()
+            barrier()
+        launches = (_C.launch_count - launches0) // max(args.steps, 1)
+        gemm = _C.gemm_events
+        _C.gemm_events = None
+        dt = max_over_ranks(ev0.elapsed_time(ev1) / 1000.0)
+        gemm_ms = sum(a.elapsed_time(b) for a, b, _ in gemm)
+        gemm_flops = sum(f for _, _, f in gemm)
+
+        # ---- end-to-end through the public API (e2e) --------------------------------
+        for _ in range(2):
+            worker.embed(ids, pos, last)
+        barrier()
+        t0 = time.perf_counter()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            out = worker.embed(ids, pos, last)
+        e1.record()
+        barrier()
+        e2e_dt = max_over_ranks(max(e0.elapsed_time(e1) / 1000.0, time.perf_counter() - t0))
+
+    err = _C.take_device_error()
+    if err:
+        raise RuntimeError(f"device error {err} during the benchmark")
+
+    peak_burst, peak_sust, hbm, peak_kind = peaks()
+    achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else 0.0
+    result = None
+    if rank == 0:
+        value = T * args.steps / dt
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            threads = os.cpu_count() or 1
+            tps, per = cpu_forward_tokens_per_s(cfg, 1000, 4, threads, repeats=1)
+            cpu = {"value": tps, "unit": UNIT, "cores": threads, "kind": "port",
+                   "sample": "1 x 1000 tokens through 4 of the layers in fp32 (CPU oracle, "
+                             "dense weights of the same shapes), time scaled to full depth"}
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt / args.steps * 1000, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded AWQ weights and token ids)",
+            "config": {"workload": desc, "tokens": T, "sequences": len(lengths),
+                       "parallelism": f"tp{world}",
+                       "l2": "inputs larger than L2 (weights + activations > 126 MB per step)"},
+            "e2e": {"value": T * args.steps / e2e_dt, "unit": UNIT,
+                    "h2d_bytes_per_step": int(ids.nbytes + pos.nbytes + last.nbytes),
+                    "d2h_bytes_per_step": int(out.numel() * 4)},
+            "gpu_launches": launches * args.steps,
+            "roofline": {"kernel": "awq_gemm (all launches in the timed region)",
+                         "bound": "tensor", "achieved": achieved, "peak": peak_sust,
+                         "peak_kind": f"{peak_kind} bf16 sustained", "unit": "TFLOP/s",
+                         "frac": achieved / peak_sust, "traffic": None,
+                         "share_of_step": gemm_ms / (dt * 1000) if dt > 0 else None},
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_mes(args)
+
+
+if __name__ == "__main__":
+    main()

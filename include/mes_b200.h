@@ -1,0 +1,171 @@
+/*
+ * mes_b200 - C ABI of the B200 (sm_100a) kernels behind the embedding server's
+ * GPU-worker forward pass.
+ *
+ * Conventions
+ *   - Every pointer is a CUDA device pointer unless stated otherwise; tensors are dense
+ *     row-major.  Element types are given per argument: bf16 = __nv_bfloat16,
+ *     f16 = __half, i32 / i64 = int32_t / int64_t, f32 = float.
+ *   - `stream` is a cudaStream_t passed as void*; work is enqueued on it and the call
+ *     returns without synchronising.  Nothing here allocates device memory: scratch
+ *     comes from the caller.
+ *   - The return value is a mes_status (0 = success).  Argument errors are detected on
+ *     the host before anything is launched.  Device-side wait limits record a code that
+ *     mes_take_device_error() returns.
+ *
+ * Each entry point names the reference interface (woodx9/minimal-embedding-server, path
+ * within that project, file:line) whose computation it replaces.
+ */
+#ifndef MES_B200_H_
+#define MES_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum mes_status {
+  MES_OK = 0,
+  MES_ERR_INVALID = 1,     /* bad size, null pointer or unsupported shape          */
+  MES_ERR_ALIGN = 2,       /* pointer or pitch violates the stated alignment       */
+  MES_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed                    */
+  MES_ERR_TIMEOUT = 4,     /* a device wait ran past its limit (see device error)  */
+  MES_ERR_UNSUPPORTED = 5  /* no sm_100a device / feature unavailable              */
+} mes_status;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int mes_version(void);
+
+/* Human-readable text for a status code (static storage). */
+const char* mes_status_string(int status);
+
+/* Returns and clears the first device-side error code recorded by any kernel of this
+ * library on the current device (0 if none).  Synchronises the current device. */
+int mes_take_device_error(int* code);
+
+/* ---------------------------------------------------------------------------------
+ * Embedding gather.  out[t, :] = table[ids[t], :].
+ * Replaces VocabParallelEmbedding.forward (layers/embed_head.py:43-52); the table is
+ * replicated per rank, so no all-reduce is needed at tp>1.
+ * ids: i64 [T] (each in [0, vocab)); table: bf16 [vocab, H]; out: bf16 [T, H]; H % 8 == 0.
+ * Out-of-range ids produce a zero row and record MES_ERR_INVALID as device error.
+ * ------------------------------------------------------------------------------- */
+int mes_embedding(const int64_t* ids, int64_t T, const void* table, int64_t vocab,
+                  int64_t H, void* out, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * RMSNorm.  y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w), statistics in fp32.
+ * Replaces RMSNorm.rms_forward (layers/layernorm.py:18-27).
+ * x, y: bf16 [rows, H] (y may alias x); w: bf16 [H]; H % 256 == 0, H <= 8192.
+ * ------------------------------------------------------------------------------- */
+int mes_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t H, float eps,
+                void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Fused residual add + RMSNorm.  s = x + residual (fp32); residual_out = bf16(s);
+ * y = bf16(bf16(s * rsqrt(mean(s^2) + eps)) * w).
+ * Replaces RMSNorm.add_rms_forward (layers/layernorm.py:30-41).
+ * x, residual: bf16 [rows, H]; y, residual_out: bf16 [rows, H].  y may alias x and
+ * residual_out may alias residual (in-place update of the residual stream).
+ * ------------------------------------------------------------------------------- */
+int mes_add_rmsnorm(const void* x, const void* residual, const void* w, void* y,
+                    void* residual_out, int64_t rows, int64_t H, float eps, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Fused per-head q/k RMSNorm + NeoX RoPE, in place on the packed QKV projection output.
+ * Replaces the q_norm/k_norm calls of Qwen3Attention.forward (models/qwen3.py:82-88) and
+ * RotaryEmbedding.forward (layers/rotary_embedding.py:39-55; Qwen2: models/qwen2.py:85).
+ * qkv: bf16 rows of pitch `ld` elements holding Hq q heads then Hkv k heads of D each
+ *      (the packed [T, (Hq + 2*Hkv) * D] projection output; its v heads are untouched).
+ *      Hq or Hkv may be 0 to rotate a q-only or k-only tensor.
+ * positions: i64 [T]; cos_sin: bf16 or f32 (cos_sin_f32 != 0) [max_pos, D] = cat(cos, sin);
+ * q_w, k_w: bf16 [D] (ignored when apply_norm == 0); D == 128.
+ * ------------------------------------------------------------------------------- */
+int mes_qknorm_rope(void* qkv, int64_t ld, const int64_t* positions, const void* cos_sin,
+                    int cos_sin_f32, int64_t max_pos, const void* q_w, const void* k_w,
+                    int64_t T, int Hq, int Hkv, int D, float eps, int apply_norm,
+                    void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * SiLU-and-mul.  y[r, i] = bf16(silu(x[r, i]) * x[r, I + i]) in fp32.
+ * Replaces SiluAndMul.forward (layers/activation.py:12-14).
+ * x: bf16 [rows, 2I]; y: bf16 [rows, I]; I % 8 == 0.
+ * ------------------------------------------------------------------------------- */
+int mes_silu_mul(const void* x, void* y, int64_t rows, int64_t I, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Sequence boundaries and attention work list for a packed varlen batch, computed on
+ * the device (no host synchronisation).  A new sequence starts at token i when
+ * positions[i] != positions[i-1] + 1 - the rule of layers/attention/flashattention.py:26-34,
+ * which the reference evaluates on the host with one .item() per boundary in every layer.
+ * positions: i64 [T].  Outputs (caller-owned scratch, see mes_varlen_workspace_size):
+ *   workspace: opaque buffer of mes_varlen_workspace_size(T) bytes, 256-byte aligned,
+ *   holding cu_seqlens (i32 [T+1]), the sequence count and the (sequence, query-tile)
+ *   work list consumed by mes_varlen_attention.
+ * ------------------------------------------------------------------------------- */
+int64_t mes_varlen_workspace_size(int64_t T);
+int mes_varlen_schedule(const int64_t* positions, int64_t T, void* workspace, void* stream);
+
+/* Copies cu_seqlens (i32 [num_seqs+1]) out of a scheduled workspace into `cu_seqlens`
+ * (device, capacity T+1) and the count into `num_seqs` (device i32 [1]). */
+int mes_varlen_cu_seqlens(const void* workspace, int64_t T, int32_t* cu_seqlens,
+                          int32_t* num_seqs, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Varlen causal GQA prefill attention on tcgen05/TMEM.
+ * out[t, h*D:(h+1)*D] = softmax_causal(q_h k_g^T * scale) v_g within t's sequence,
+ * g = h / (Hq / Hkv).  Replaces FlashAttention.forward / FlashInferAttention.forward
+ * (layers/attention/flashattention.py:19-48, layers/attention/flashinfer.py:55-101).
+ * qkv: bf16 [T, (Hq + 2*Hkv) * D] (pitch `ld` elements, ld % 8 == 0, 16-byte aligned);
+ * out: bf16 [T, Hq * D]; D == 128; workspace from mes_varlen_schedule on the same
+ * positions.
+ * ------------------------------------------------------------------------------- */
+int mes_varlen_attention(const void* qkv, int64_t ld, void* out, const void* workspace,
+                         int64_t T, int Hq, int Hkv, int D, float scale, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Last-token pooling + L2 normalisation.  out[b, :] = x / max(||x||_2, 1e-12),
+ * x = hidden[idx[b], :] (fp32 math and output).
+ * Replaces the post-process of GPUWorker._inference_worker (core/gpu_worker.py:252-261)
+ * and ultils/pool.py:4-9.
+ * hidden: bf16 [T, H]; idx: i64 [B]; out: f32 [B, H]; H % 8 == 0.
+ * ------------------------------------------------------------------------------- */
+int mes_last_token_l2(const void* hidden, int64_t T, int64_t H, const int64_t* idx,
+                      int64_t B, float* out, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * AWQ int4 weights.  Checkpoint format (AutoAWQ GEMM layout): qweight i32 [K, N/8] with
+ * nibble i of word (k, j) = code of column 8j + {0,2,4,6,1,3,5,7}[i]; qzeros i32
+ * [K/G, N/8] packed the same way; scales f16 [K/G, N]; group size G = 128.
+ * Dequantised value: w[k, n] = (q - z) * s, exact in fp32, rounded once to bf16 (RNE).
+ * The reference holds dense weights and calls F.linear (layers/linear.py:54,86,179);
+ * these entry points replace that GEMM for QKVParallelLinear, MergedColumnParallelLinear
+ * and RowParallelLinear (layers/linear.py:90-180).
+ * ------------------------------------------------------------------------------- */
+
+/* Repacks a checkpoint qweight [K, N/8] into the kernel layout i32 [K/8, N] (the same
+ * nibble interleave applied along K).  Lossless; run once at load time.
+ * K % 128 == 0, N % 8 == 0. */
+int mes_awq_repack(const int32_t* qweight, int64_t K, int64_t N, int32_t* qweight_mes,
+                   void* stream);
+
+/* Dequantises the kernel layout to bf16 W^T [N, K] (row n = output feature n) using the
+ * same arithmetic as the GEMM.  For verification. */
+int mes_awq_dequant(const int32_t* qweight_mes, const int32_t* qzeros, const void* scales,
+                    int64_t K, int64_t N, int group_size, void* w_out, void* stream);
+
+/* Y[M, N] = X[M, K] * W[K, N] (+ bias[N]), W from AWQ (kernel layout), fp32 accumulate
+ * on tcgen05, bf16 output.  X: bf16 [M, K] (pitch ldx elements); Y: bf16 [M, N] (pitch
+ * ldy); bias: bf16 [N] or NULL; scales: f16 [K/G, N]; qzeros: i32 [K/G, N/8].
+ * Requirements: N % 128 == 0, K % 128 == 0, group_size == 128, ldx/ldy % 8 == 0,
+ * X/Y 16-byte aligned.  M may be any value >= 0. */
+int mes_awq_gemm(const void* X, int64_t ldx, const int32_t* qweight_mes,
+                 const int32_t* qzeros, const void* scales, const void* bias, void* Y,
+                 int64_t ldy, int64_t M, int64_t N, int64_t K, int group_size, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MES_B200_H_ */

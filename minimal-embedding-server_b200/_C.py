@@ -1,0 +1,265 @@
+"""ctypes binding of ``lib/libmes_b200.so`` (the C ABI declared in ``include/mes_b200.h``).
+
+Every function here takes torch CUDA tensors, checks shapes/dtypes on the host, passes
+raw device pointers plus the current CUDA stream to the library and raises
+:class:`MesError` on a non-zero status.  There is no fallback: if the library is missing,
+fails to load, or no CUDA device is present, the call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libmes_b200.so")
+
+_vp, _i64, _i32, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
+
+# name -> (restype, argtypes); mirrors include/mes_b200.h
+SIGNATURES = {
+    "mes_version": (_i32, []),
+    "mes_status_string": (ctypes.c_char_p, [_i32]),
+    "mes_take_device_error": (_i32, [ctypes.POINTER(_i32)]),
+    "mes_embedding": (_i32, [_vp, _i64, _vp, _i64, _i64, _vp, _vp]),
+    "mes_rmsnorm": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _vp]),
+    "mes_add_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
+    "mes_qknorm_rope": (_i32, [_vp, _i64, _vp, _vp, _i32, _i64, _vp, _vp, _i64, _i32, _i32,
+                               _i32, _f32, _i32, _vp]),
+    "mes_silu_mul": (_i32, [_vp, _vp, _i64, _i64, _vp]),
+    "mes_varlen_workspace_size": (_i64, [_i64]),
+    "mes_varlen_schedule": (_i32, [_vp, _i64, _vp, _vp]),
+    "mes_varlen_cu_seqlens": (_i32, [_vp, _i64, _vp, _vp, _vp]),
+    "mes_varlen_attention": (_i32, [_vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp]),
+    "mes_last_token_l2": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _vp]),
+    "mes_awq_repack": (_i32, [_vp, _i64, _i64, _vp, _vp]),
+    "mes_awq_dequant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp]),
+    "mes_awq_gemm": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32,
+                            _vp]),
+}
+
+_lib = None
+
+# Number of kernel launches issued through this module (each wrapper below launches
+# exactly one kernel); read by the benchmark to report its launch count.
+launch_count = 0
+
+# Optional per-launch timing hook for the AWQ GEMM: when set to a list, every awq_gemm
+# call appends (start_event, end_event, flops) recorded on the launching stream.
+gemm_events = None
+
+
+class MesError(RuntimeError):
+    """A mes_b200 library call returned a non-zero status."""
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the CUDA library; raises if it is not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise MesError(f"mes_b200 CUDA library not found at {LIB_PATH}; "
+                           "build it with __graft_entry__.build()")
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = handle
+    return _lib
+
+
+def status_string(code: int) -> str:
+    return lib().mes_status_string(code).decode()
+
+
+def _check(code: int, what: str, launches: int = 1) -> None:
+    global launch_count
+    if code != 0:
+        raise MesError(f"{what}: {status_string(code)} (status {code})")
+    launch_count += launches
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(t: torch.Tensor):
+    if not t.is_cuda:
+        raise MesError("mes_b200 kernels need CUDA tensors (there is no CPU path)")
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise MesError(msg)
+
+
+def take_device_error() -> int:
+    code = _i32(0)
+    _check(lib().mes_take_device_error(ctypes.byref(code)), "mes_take_device_error", 0)
+    return code.value
+
+
+# --------------------------------------------------------------------------------------
+# torch-facing wrappers
+# --------------------------------------------------------------------------------------
+def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None):
+    _need(ids.dtype == torch.int64 and ids.dim() == 1, "ids must be int64 [T]")
+    _need(table.dtype == torch.bfloat16 and table.dim() == 2 and table.is_contiguous(),
+          "table must be contiguous bf16 [vocab, H]")
+    T, (V, H) = ids.shape[0], table.shape
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=table.device)
+    ids = ids.contiguous()
+    _check(lib().mes_embedding(_p(ids), T, _p(table), V, H, _p(out), _stream(table)),
+           "mes_embedding")
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None):
+    _need(x.dtype == torch.bfloat16 and x.is_contiguous(), "x must be contiguous bf16")
+    H = x.shape[-1]
+    out = torch.empty_like(x) if out is None else out
+    _check(lib().mes_rmsnorm(_p(x), _p(w), _p(out), x.numel() // H, H, eps, _stream(x)),
+           "mes_rmsnorm")
+    return out
+
+
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                out: torch.Tensor | None = None, residual_out: torch.Tensor | None = None):
+    _need(x.dtype == torch.bfloat16 and residual.dtype == torch.bfloat16, "bf16 inputs")
+    _need(x.is_contiguous() and residual.is_contiguous() and x.shape == residual.shape,
+          "x and residual must be contiguous and of one shape")
+    H = x.shape[-1]
+    out = torch.empty_like(x) if out is None else out
+    residual_out = torch.empty_like(residual) if residual_out is None else residual_out
+    _check(lib().mes_add_rmsnorm(_p(x), _p(residual), _p(w), _p(out), _p(residual_out),
+                                 x.numel() // H, H, eps, _stream(x)), "mes_add_rmsnorm")
+    return out, residual_out
+
+
+def qknorm_rope(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
+                num_q_heads: int, num_k_heads: int, head_dim: int,
+                q_weight: torch.Tensor | None = None, k_weight: torch.Tensor | None = None,
+                eps: float = 1e-6) -> torch.Tensor:
+    """In place on ``qkv`` (rows of pitch ``qkv.stride(0)``): optional per-head RMSNorm of
+    the first ``num_q_heads`` (weight ``q_weight``) and next ``num_k_heads`` heads
+    (``k_weight``), then NeoX RoPE with ``cos_sin[positions]``."""
+    _need(qkv.dtype == torch.bfloat16 and qkv.stride(-1) == 1, "qkv must be bf16, unit stride")
+    _need(positions.dtype == torch.int64, "positions must be int64")
+    _need(cos_sin.dtype in (torch.float32, torch.bfloat16) and cos_sin.is_contiguous(),
+          "cos_sin must be a contiguous fp32/bf16 cache")
+    apply_norm = q_weight is not None or k_weight is not None
+    T = positions.shape[0]
+    _check(lib().mes_qknorm_rope(_p(qkv), qkv.stride(0), _p(positions.contiguous()),
+                                 _p(cos_sin), int(cos_sin.dtype == torch.float32),
+                                 cos_sin.shape[0], _p(q_weight), _p(k_weight), T, num_q_heads,
+                                 num_k_heads, head_dim, eps, int(apply_norm), _stream(qkv)),
+           "mes_qknorm_rope")
+    return qkv
+
+
+def silu_mul(x: torch.Tensor, out: torch.Tensor | None = None):
+    _need(x.dtype == torch.bfloat16 and x.is_contiguous() and x.shape[-1] % 2 == 0,
+          "x must be contiguous bf16 [..., 2I]")
+    I = x.shape[-1] // 2
+    if out is None:
+        out = torch.empty(*x.shape[:-1], I, dtype=x.dtype, device=x.device)
+    _check(lib().mes_silu_mul(_p(x), _p(out), x.numel() // (2 * I), I, _stream(x)),
+           "mes_silu_mul")
+    return out
+
+
+def varlen_workspace_size(T: int) -> int:
+    return int(lib().mes_varlen_workspace_size(T))
+
+
+def varlen_schedule(positions: torch.Tensor, workspace: torch.Tensor | None = None):
+    _need(positions.dtype == torch.int64 and positions.dim() == 1, "positions must be int64 [T]")
+    T = positions.shape[0]
+    size = varlen_workspace_size(T)
+    if workspace is None:
+        workspace = torch.empty(size, dtype=torch.uint8, device=positions.device)
+    _need(workspace.numel() >= size, "workspace too small")
+    positions = positions.contiguous()
+    _check(lib().mes_varlen_schedule(_p(positions), T, _p(workspace), _stream(positions)),
+           "mes_varlen_schedule")
+    return workspace
+
+
+def varlen_cu_seqlens(workspace: torch.Tensor, T: int):
+    cu = torch.empty(T + 1, dtype=torch.int32, device=workspace.device)
+    n = torch.empty(1, dtype=torch.int32, device=workspace.device)
+    _check(lib().mes_varlen_cu_seqlens(_p(workspace), T, _p(cu), _p(n), _stream(workspace)),
+           "mes_varlen_cu_seqlens", 0)
+    return cu, n
+
+
+def varlen_attention(qkv: torch.Tensor, workspace: torch.Tensor, num_heads: int,
+                     num_kv_heads: int, head_dim: int, scale: float,
+                     out: torch.Tensor | None = None):
+    _need(qkv.dtype == torch.bfloat16 and qkv.stride(-1) == 1, "qkv must be bf16, unit stride")
+    T = qkv.shape[0]
+    if out is None:
+        out = torch.empty(T, num_heads * head_dim, dtype=torch.bfloat16, device=qkv.device)
+    _check(lib().mes_varlen_attention(_p(qkv), qkv.stride(0), _p(out), _p(workspace), T,
+                                      num_heads, num_kv_heads, head_dim, scale, _stream(qkv)),
+           "mes_varlen_attention")
+    return out
+
+
+def last_token_l2(hidden: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = None):
+    _need(hidden.dtype == torch.bfloat16 and hidden.is_contiguous() and hidden.dim() == 2,
+          "hidden must be contiguous bf16 [T, H]")
+    _need(idx.dtype == torch.int64, "indices must be int64")
+    T, H = hidden.shape
+    B = idx.shape[0]
+    if out is None:
+        out = torch.empty(B, H, dtype=torch.float32, device=hidden.device)
+    _check(lib().mes_last_token_l2(_p(hidden), T, H, _p(idx.contiguous()), B, _p(out),
+                                   _stream(hidden)), "mes_last_token_l2")
+    return out
+
+
+def awq_repack(qweight: torch.Tensor) -> torch.Tensor:
+    _need(qweight.dtype == torch.int32 and qweight.dim() == 2 and qweight.is_contiguous(),
+          "qweight must be contiguous int32 [K, N/8]")
+    K, N = qweight.shape[0], qweight.shape[1] * 8
+    out = torch.empty(K // 8, N, dtype=torch.int32, device=qweight.device)
+    _check(lib().mes_awq_repack(_p(qweight), K, N, _p(out), _stream(qweight)), "mes_awq_repack")
+    return out
+
+
+def awq_dequant(qweight_mes: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
+                group_size: int = 128) -> torch.Tensor:
+    """bf16 W^T [N, K] with the GEMM's exact dequantisation (for verification)."""
+    K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
+    out = torch.empty(N, K, dtype=torch.bfloat16, device=qweight_mes.device)
+    _check(lib().mes_awq_dequant(_p(qweight_mes), _p(qzeros), _p(scales), K, N, group_size,
+                                 _p(out), _stream(qweight_mes)), "mes_awq_dequant")
+    return out
+
+
+def awq_gemm(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
+             scales: torch.Tensor, bias: torch.Tensor | None = None,
+             out: torch.Tensor | None = None, group_size: int = 128) -> torch.Tensor:
+    """``x[M, K] @ W[K, N] (+ bias)`` with W given by AWQ tensors in the kernel layout."""
+    _need(x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(-1) == 1,
+          "x must be bf16 [M, K] with unit inner stride")
+    K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
+    M = x.shape[0]
+    _need(x.shape[1] == K, f"x has K={x.shape[1]}, weight has K={K}")
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    ev = gemm_events
+    if ev is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+    _check(lib().mes_awq_gemm(_p(x), x.stride(0), _p(qweight_mes), _p(qzeros), _p(scales),
+                              _p(bias), _p(out), out.stride(0), M, N, K, group_size,
+                              _stream(x)), "mes_awq_gemm")
+    if ev is not None:
+        e1.record()
+        ev.append((e0, e1, 2.0 * M * N * K))
+    return out

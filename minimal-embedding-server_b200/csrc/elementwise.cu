@@ -1,0 +1,446 @@
+// Memory-bound kernels of the forward pass: embedding gather, RMSNorm, fused
+// add+RMSNorm, fused per-head q/k RMSNorm + NeoX RoPE, SiLU-and-mul, last-token
+// pooling + L2 normalisation, and the on-device varlen schedule.
+//
+// All of them move 16-byte vectors (8 bf16) with coalesced loads/stores and reduce with
+// warp shuffles; statistics and transcendental math are fp32.
+#include "common.cuh"
+
+namespace {
+
+__device__ int g_err_elementwise = 0;
+
+using bf162 = __nv_bfloat162;
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const bf162* h = reinterpret_cast<const bf162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 v;
+  uint32_t* u = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) u[i] = mes::pack_bf16x2(f[2 * i], f[2 * i + 1]);
+  return v;
+}
+// Round fp32 to bf16 and back (the reference's `.to(orig_dtype)` before `* weight`).
+__device__ __forceinline__ float round_bf16(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide sum for blockDim.x <= 1024; every thread gets the result.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (l < nw) ? red[l] : 0.f;
+  t = warp_sum(t);
+  __syncthreads();
+  return t;
+}
+
+// ------------------------------------ embedding ----------------------------------------
+__global__ void embedding_kernel(const int64_t* __restrict__ ids, int64_t T,
+                                 const uint4* __restrict__ table, int64_t vocab, int64_t hv,
+                                 uint4* __restrict__ out) {
+  const int64_t total = T * hv;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / hv, c = i - t * hv;
+    const int64_t id = __ldg(ids + t);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (id >= 0 && id < vocab) {
+      v = __ldg(table + id * hv + c);
+    } else if (c == 0) {
+      atomicCAS(&g_err_elementwise, 0, MES_ERR_INVALID);
+    }
+    out[i] = v;
+  }
+}
+
+// ------------------------------------- RMSNorm -----------------------------------------
+// One block per row, one 8-element vector per thread (blockDim.x = H / 8).
+template <bool kAdd>
+__global__ void rmsnorm_kernel(const uint4* x, const uint4* residual, const uint4* __restrict__ w,
+                               uint4* y, uint4* residual_out, int hv, float inv_h, float eps) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int c = threadIdx.x;
+  float f[8];
+  unpack8(x[row * hv + c], f);
+  if (kAdd) {
+    float r[8];
+    unpack8(residual[row * hv + c], r);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] += r[i];
+    residual_out[row * hv + c] = pack8(f);  // new residual = bf16(x + r)
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+  ss = block_sum(ss, red);
+  const float rs = rsqrtf(ss * inv_h + eps);
+  float wf[8];
+  unpack8(w[c], wf);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = round_bf16(f[i] * rs) * wf[i];
+  y[row * hv + c] = pack8(f);
+}
+
+// ------------------------------ q/k RMSNorm + NeoX RoPE --------------------------------
+// 16 threads per (token, head): thread j holds elements 8j..8j+7 of the 128-wide head.
+// The rotate-half partner of thread j is j ^ 8.
+template <bool kNorm, bool kF32Cache>
+__global__ void qknorm_rope_kernel(bf162* __restrict__ qkv, int64_t ld, const int64_t* __restrict__ pos,
+                                   const void* __restrict__ cos_sin, int64_t max_pos,
+                                   const uint4* __restrict__ qw, const uint4* __restrict__ kw,
+                                   int64_t T, int Hq, int Hkv, float eps) {
+  const int nh = Hq + Hkv;
+  const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t item = gid >> 4;  // (token, head)
+  const int j = threadIdx.x & 15;
+  const bool valid = item < T * nh;
+  const int64_t t = valid ? item / nh : 0;
+  const int h = valid ? (int)(item - t * nh) : 0;
+  uint4* rowp = reinterpret_cast<uint4*>(qkv + (t * ld) / 2) + h * 16 + j;
+  float f[8];
+  uint4 raw = valid ? *rowp : make_uint4(0, 0, 0, 0);
+  unpack8(raw, f);
+  if (kNorm) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rs = rsqrtf(ss * (1.0f / 128.0f) + eps);
+    float wf[8];
+    unpack8((h < Hq ? qw : kw)[j], wf);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = round_bf16(round_bf16(f[i] * rs) * wf[i]);
+  }
+  float p[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = __shfl_xor_sync(0xffffffffu, f[i], 8);
+  int64_t ps = valid ? __ldg(pos + t) : 0;
+  if (ps < 0 || ps >= max_pos) {
+    if (valid && j == 0) atomicCAS(&g_err_elementwise, 0, MES_ERR_INVALID);
+    ps = 0;
+  }
+  const int cj = (j & 7) * 8;  // cos/sin column of this thread's first element
+  float c[8], s[8];
+  if (kF32Cache) {
+    const float4* cs = reinterpret_cast<const float4*>(
+        static_cast<const float*>(cos_sin) + ps * 128);
+    float4 a = __ldg(cs + cj / 4), b = __ldg(cs + cj / 4 + 1);
+    float4 d = __ldg(cs + 16 + cj / 4), e = __ldg(cs + 16 + cj / 4 + 1);
+    c[0] = a.x; c[1] = a.y; c[2] = a.z; c[3] = a.w; c[4] = b.x; c[5] = b.y; c[6] = b.z; c[7] = b.w;
+    s[0] = d.x; s[1] = d.y; s[2] = d.z; s[3] = d.w; s[4] = e.x; s[5] = e.y; s[6] = e.z; s[7] = e.w;
+  } else {
+    const uint4* cs = reinterpret_cast<const uint4*>(
+        static_cast<const __nv_bfloat16*>(cos_sin) + ps * 128);
+    unpack8(__ldg(cs + cj / 8), c);
+    unpack8(__ldg(cs + 8 + cj / 8), s);
+  }
+  float o[8];
+  if (j < 8) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = f[i] * c[i] - p[i] * s[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = f[i] * c[i] + p[i] * s[i];
+  }
+  if (valid) *rowp = pack8(o);
+}
+
+// ------------------------------------ SiLU-and-mul -------------------------------------
+__global__ void silu_mul_kernel(const uint4* __restrict__ x, uint4* __restrict__ y,
+                                int64_t rows, int64_t iv) {
+  const int64_t total = rows * iv;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / iv, c = i - r * iv;
+    float g[8], u[8];
+    unpack8(__ldg(x + r * 2 * iv + c), g);
+    unpack8(__ldg(x + r * 2 * iv + iv + c), u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) g[k] = g[k] / (1.0f + expf(-g[k])) * u[k];
+    y[i] = pack8(g);
+  }
+}
+
+// ------------------------------ last token + L2 normalise ------------------------------
+__global__ void last_token_l2_kernel(const uint4* __restrict__ hidden, int64_t T, int hv,
+                                     const int64_t* __restrict__ idx, float4* __restrict__ out) {
+  __shared__ float red[32];
+  const int64_t b = blockIdx.x;
+  int64_t t = __ldg(idx + b);
+  const bool ok = t >= 0 && t < T;
+  if (!ok) {
+    if (threadIdx.x == 0) atomicCAS(&g_err_elementwise, 0, MES_ERR_INVALID);
+    t = 0;
+  }
+  float ss = 0.f;
+  float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int c = threadIdx.x; c < hv; c += blockDim.x) {
+    unpack8(__ldg(hidden + t * hv + c), f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+  }
+  ss = block_sum(ss, red);
+  const float inv = ok ? 1.0f / fmaxf(sqrtf(ss), 1e-12f) : 0.f;
+  for (int c = threadIdx.x; c < hv; c += blockDim.x) {
+    unpack8(__ldg(hidden + t * hv + c), f);
+    out[(b * hv + c) * 2] = make_float4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
+    out[(b * hv + c) * 2 + 1] = make_float4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv);
+  }
+}
+
+// -------------------------------- varlen schedule --------------------------------------
+// Workspace layout (bytes): [0,4) num_seqs, [4,8) num_tile_items, [8,12) max_tiles,
+// [256, 256 + 4(T+1)) cu_seqlens, then (aligned to 256) the tile items int2 {seq, qtile}
+// ordered by descending qtile (longest causal rows first), capacity T + T/128 + 1.
+constexpr int kSchedThreads = 1024;
+constexpr int kQTile = 128;
+
+__device__ __forceinline__ int block_excl_scan(int v, int* sm, int* total) {
+  // Inclusive warp scan, then across warps.
+  const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (l >= o) x += y;
+  }
+  if (l == 31) sm[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    int s = sm[l];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (l >= o) s += y;
+    }
+    sm[l] = s;
+  }
+  __syncthreads();
+  const int before = (w > 0 ? sm[w - 1] : 0) + x - v;
+  *total = sm[31];
+  __syncthreads();
+  return before;
+}
+
+__global__ void __launch_bounds__(kSchedThreads)
+varlen_schedule_kernel(const int64_t* __restrict__ pos, int T, int* __restrict__ hdr,
+                       int* __restrict__ cu, int2* __restrict__ items) {
+  __shared__ int sm[32];
+  __shared__ int s_maxtiles;
+  // Pass 1: sequence starts -> cu_seqlens.
+  int base = 0;
+  for (int c0 = 0; c0 < T; c0 += kSchedThreads) {
+    const int i = c0 + threadIdx.x;
+    int start = 0;
+    if (i < T) start = (i == 0) || (pos[i] != pos[i - 1] + 1);
+    int total;
+    const int ex = block_excl_scan(start, sm, &total);
+    if (start) cu[base + ex] = i;
+    base += total;
+  }
+  const int B = base;
+  if (threadIdx.x == 0) {
+    cu[B] = T;
+    hdr[0] = B;
+    s_maxtiles = 0;
+  }
+  __syncthreads();
+  // Pass 2: longest sequence in tiles.
+  int mt = 0;
+  for (int s = threadIdx.x; s < B; s += kSchedThreads)
+    mt = max(mt, (cu[s + 1] - cu[s] + kQTile - 1) / kQTile);
+  atomicMax(&s_maxtiles, mt);
+  __syncthreads();
+  const int J = s_maxtiles;
+  // Pass 3: items ordered by descending tile index, sequences ascending within a tile.
+  int n = 0;
+  for (int j = J - 1; j >= 0; --j) {
+    for (int c0 = 0; c0 < B; c0 += kSchedThreads) {
+      const int s = c0 + threadIdx.x;
+      int has = 0;
+      if (s < B) has = (cu[s + 1] - cu[s] + kQTile - 1) / kQTile > j;
+      int total;
+      const int ex = block_excl_scan(has, sm, &total);
+      if (has) items[n + ex] = make_int2(s, j);
+      n += total;
+    }
+  }
+  if (threadIdx.x == 0) {
+    hdr[1] = n;
+    hdr[2] = J;
+  }
+}
+
+inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+inline int64_t cu_offset() { return 256; }
+inline int64_t items_offset(int64_t T) { return align256(cu_offset() + 4 * (T + 1)); }
+inline int64_t items_capacity(int64_t T) { return T + T / kQTile + 1; }
+
+inline int grid_for(int64_t work, int threads) {
+  int64_t b = (work + threads - 1) / threads;
+  const int64_t cap = (int64_t)mes_host::sm_count() * 32;
+  if (b > cap) b = cap;
+  return (int)(b < 1 ? 1 : b);
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+// =========================================================================================
+// C ABI
+// =========================================================================================
+extern "C" int mes_elementwise_take_error(int* code) {
+  int v = 0, zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_err_elementwise, sizeof(int));
+  if (e != cudaSuccess) return MES_ERR_CUDA;
+  e = cudaMemcpyToSymbol(g_err_elementwise, &zero, sizeof(int));
+  *code = v;
+  return mes_host::from_cuda(e);
+}
+
+extern "C" int mes_embedding(const int64_t* ids, int64_t T, const void* table, int64_t vocab,
+                             int64_t H, void* out, void* stream) {
+  if (T < 0 || vocab <= 0 || H <= 0 || H % 8) return MES_ERR_INVALID;
+  if (T == 0) return MES_OK;
+  if (!ids || !table || !out) return MES_ERR_INVALID;
+  if (!aligned16(table) || !aligned16(out)) return MES_ERR_ALIGN;
+  const int64_t hv = H / 8;
+  embedding_kernel<<<grid_for(T * hv, 256), 256, 0, (cudaStream_t)stream>>>(
+      ids, T, (const uint4*)table, vocab, hv, (uint4*)out);
+  return mes_host::from_cuda(cudaGetLastError());
+}
+
+static int launch_rmsnorm(bool add, const void* x, const void* residual, const void* w, void* y,
+                          void* residual_out, int64_t rows, int64_t H, float eps, void* stream) {
+  if (rows < 0 || H <= 0 || H % 256 || H / 8 > 1024) return MES_ERR_INVALID;
+  if (rows == 0) return MES_OK;
+  if (!x || !w || !y || (add && (!residual || !residual_out))) return MES_ERR_INVALID;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y) ||
+      (add && (!aligned16(residual) || !aligned16(residual_out))))
+    return MES_ERR_ALIGN;
+  if (rows > 0x7fffffffLL) return MES_ERR_INVALID;
+  const int hv = (int)(H / 8);
+  if (add)
+    rmsnorm_kernel<true><<<(unsigned)rows, hv, 0, (cudaStream_t)stream>>>(
+        (const uint4*)x, (const uint4*)residual, (const uint4*)w, (uint4*)y, (uint4*)residual_out,
+        hv, 1.0f / (float)H, eps);
+  else
+    rmsnorm_kernel<false><<<(unsigned)rows, hv, 0, (cudaStream_t)stream>>>(
+        (const uint4*)x, nullptr, (const uint4*)w, (uint4*)y, nullptr, hv, 1.0f / (float)H, eps);
+  return mes_host::from_cuda(cudaGetLastError());
+}
+
+extern "C" int mes_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t H,
+                           float eps, void* stream) {
+  return launch_rmsnorm(false, x, nullptr, w, y, nullptr, rows, H, eps, stream);
+}
+
+extern "C" int mes_add_rmsnorm(const void* x, const void* residual, const void* w, void* y,
+                               void* residual_out, int64_t rows, int64_t H, float eps,
+                               void* stream) {
+  return launch_rmsnorm(true, x, residual, w, y, residual_out, rows, H, eps, stream);
+}
+
+extern "C" int mes_qknorm_rope(void* qkv, int64_t ld, const int64_t* positions,
+                               const void* cos_sin, int cos_sin_f32, int64_t max_pos,
+                               const void* q_w, const void* k_w, int64_t T, int Hq, int Hkv,
+                               int D, float eps, int apply_norm, void* stream) {
+  if (D != 128 || T < 0 || Hq < 0 || Hkv < 0 || Hq + Hkv == 0 || max_pos <= 0) return MES_ERR_INVALID;
+  if (ld < (int64_t)(Hq + Hkv) * D || ld % 8) return MES_ERR_INVALID;
+  if (T == 0) return MES_OK;
+  if (!qkv || !positions || !cos_sin) return MES_ERR_INVALID;
+  if (apply_norm && ((Hq > 0 && !q_w) || (Hkv > 0 && !k_w))) return MES_ERR_INVALID;
+  if (!aligned16(qkv) || !aligned16(cos_sin) || (apply_norm && (!aligned16(q_w) || !aligned16(k_w))))
+    return MES_ERR_ALIGN;
+  const int64_t threads = T * (Hq + Hkv) * 16;
+  const int64_t blocks = (threads + 255) / 256;
+  cudaStream_t s = (cudaStream_t)stream;
+  bf162* p = (bf162*)qkv;
+  if (apply_norm) {
+    if (cos_sin_f32)
+      qknorm_rope_kernel<true, true><<<(unsigned)blocks, 256, 0, s>>>(
+          p, ld, positions, cos_sin, max_pos, (const uint4*)q_w, (const uint4*)k_w, T, Hq, Hkv, eps);
+    else
+      qknorm_rope_kernel<true, false><<<(unsigned)blocks, 256, 0, s>>>(
+          p, ld, positions, cos_sin, max_pos, (const uint4*)q_w, (const uint4*)k_w, T, Hq, Hkv, eps);
+  } else {
+    if (cos_sin_f32)
+      qknorm_rope_kernel<false, true><<<(unsigned)blocks, 256, 0, s>>>(
+          p, ld, positions, cos_sin, max_pos, nullptr, nullptr, T, Hq, Hkv, eps);
+    else
+      qknorm_rope_kernel<false, false><<<(unsigned)blocks, 256, 0, s>>>(
+          p, ld, positions, cos_sin, max_pos, nullptr, nullptr, T, Hq, Hkv, eps);
+  }
+  return mes_host::from_cuda(cudaGetLastError());
+}
+
+extern "C" int mes_silu_mul(const void* x, void* y, int64_t rows, int64_t I, void* stream) {
+  if (rows < 0 || I <= 0 || I % 8) return MES_ERR_INVALID;
+  if (rows == 0) return MES_OK;
+  if (!x || !y) return MES_ERR_INVALID;
+  if (!aligned16(x) || !aligned16(y)) return MES_ERR_ALIGN;
+  const int64_t iv = I / 8;
+  silu_mul_kernel<<<grid_for(rows * iv, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const uint4*)x, (uint4*)y, rows, iv);
+  return mes_host::from_cuda(cudaGetLastError());
+}
+
+extern "C" int mes_last_token_l2(const void* hidden, int64_t T, int64_t H, const int64_t* idx,
+                                 int64_t B, float* out, void* stream) {
+  if (T < 0 || H <= 0 || H % 8 || B < 0) return MES_ERR_INVALID;
+  if (B == 0) return MES_OK;
+  if (!hidden || !idx || !out || T == 0) return MES_ERR_INVALID;
+  if (!aligned16(hidden) || !aligned16(out)) return MES_ERR_ALIGN;
+  const int hv = (int)(H / 8);
+  const int threads = hv >= 256 ? 256 : ((hv + 31) / 32) * 32;
+  last_token_l2_kernel<<<(unsigned)B, threads, 0, (cudaStream_t)stream>>>(
+      (const uint4*)hidden, T, hv, idx, (float4*)out);
+  return mes_host::from_cuda(cudaGetLastError());
+}
+
+extern "C" int64_t mes_varlen_workspace_size(int64_t T) {
+  if (T < 0) return -1;
+  return items_offset(T) + 8 * items_capacity(T);
+}
+
+extern "C" int mes_varlen_schedule(const int64_t* positions, int64_t T, void* workspace,
+                                   void* stream) {
+  if (T <= 0 || T > 0x3fffffffLL || !positions || !workspace) return MES_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return MES_ERR_ALIGN;
+  char* ws = static_cast<char*>(workspace);
+  varlen_schedule_kernel<<<1, kSchedThreads, 0, (cudaStream_t)stream>>>(
+      positions, (int)T, (int*)ws, (int*)(ws + cu_offset()), (int2*)(ws + items_offset(T)));
+  return mes_host::from_cuda(cudaGetLastError());
+}
+
+extern "C" int mes_varlen_cu_seqlens(const void* workspace, int64_t T, int32_t* cu_seqlens,
+                                     int32_t* num_seqs, void* stream) {
+  if (T <= 0 || !workspace || !cu_seqlens || !num_seqs) return MES_ERR_INVALID;
+  const char* ws = static_cast<const char*>(workspace);
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemcpyAsync(cu_seqlens, ws + cu_offset(), 4 * (T + 1),
+                                  cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(num_seqs, ws, 4, cudaMemcpyDeviceToDevice, s);
+  return mes_host::from_cuda(e);
+}

@@ -1,0 +1,217 @@
+"""Parity of each CUDA kernel (called through the C ABI) against the CPU oracle."""
+import numpy as np
+import pytest
+import torch
+
+from mes_b200 import _C, synthetic
+from oracle import awq as oawq
+from oracle import ops
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def bf16(x):
+    return x.to(torch.bfloat16)
+
+
+def ulp_diff(a: torch.Tensor, b: torch.Tensor) -> int:
+    """Largest distance between two bf16 tensors in units in the last place."""
+    def key(t):
+        i = t.to(torch.bfloat16).view(torch.int16).to(torch.int64)
+        return torch.where(i < 0, -(i & 0x7FFF), i)
+    return int((key(a) - key(b)).abs().max())
+
+
+def ulp_close(a: torch.Tensor, b: torch.Tensor, ulps: int = 1) -> bool:
+    d = ulp_diff(a, b)
+    assert d <= ulps, f"{d} ulps apart (allowed {ulps})"
+    return True
+
+
+def test_no_device_error_at_start():
+    assert _C.take_device_error() == 0
+
+
+# ------------------------------------------------------------------------------ AWQ
+@pytest.mark.parametrize("K,N,seed", [(128, 128, 0), (256, 384, 1), (1024, 1024, 2)])
+def test_awq_repack_and_dequant_bit_exact(K, N, seed):
+    qw, qz, sc = oawq.random_awq(K, N, seed=seed)
+    qw_mes = _C.awq_repack(torch.from_numpy(qw).to(DEV))
+    assert np.array_equal(qw_mes.cpu().numpy(), oawq.mes_repack(qw))
+    w = _C.awq_dequant(qw_mes, torch.from_numpy(qz).to(DEV),
+                       torch.from_numpy(sc).view(torch.int16).to(DEV))
+    want = oawq.dequant_bf16_bits(qw, qz, sc)          # [K, N] bf16 bits
+    got = w.cpu().view(torch.int16).numpy().view(np.uint16).T  # W^T [N, K] -> [K, N]
+    assert np.array_equal(got, want)
+
+
+def test_awq_dequant_exhaustive_codes_and_edge_scales():
+    # every (q, z) pair against scales covering rounding ties, subnormal fp16, tiny/huge
+    K, N = 256, 256
+    q = np.tile(np.arange(16, dtype=np.uint8), (K, N // 16))
+    rng = np.random.default_rng(7)
+    q = rng.permuted(q, axis=1)
+    z = np.repeat(np.arange(16, dtype=np.uint8)[None, :], K // 128 * N // 16, 0).reshape(K // 128, N)
+    edge = np.array([1e-7, 6e-8, 6.1e-5, 0.002, 0.00201, 0.0199, 0.02, 0.5, 1.0, 1.0009766,
+                     3.14159, 65504.0, 0.33333, 0.1, 7e-3, 2.0 ** -14], dtype=np.float16)
+    s = rng.choice(edge, size=(K // 128, N)).astype(np.float16)
+    qw, qz = oawq.awq_pack(q), oawq.awq_pack(z)
+    qw_mes = _C.awq_repack(torch.from_numpy(qw).to(DEV))
+    w = _C.awq_dequant(qw_mes, torch.from_numpy(qz).to(DEV), torch.from_numpy(s).view(torch.int16).to(DEV))
+    got = w.cpu().view(torch.int16).numpy().view(np.uint16).T
+    assert np.array_equal(got, oawq.dequant_bf16_bits(qw, qz, s))
+
+
+def _gemm_case(M, K, N, bias, seed):
+    qw, qz, sc = oawq.random_awq(K, N, seed=seed)
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    b = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16) if bias else None
+    w = torch.from_numpy(oawq.bf16_bits_to_f32(oawq.dequant_bf16_bits(qw, qz, sc)))  # [K, N]
+    ref = x.float() @ w
+    if b is not None:
+        ref = ref + b.float()
+    qw_mes = _C.awq_repack(torch.from_numpy(qw).to(DEV))
+    y = _C.awq_gemm(x.to(DEV), qw_mes, torch.from_numpy(qz).to(DEV),
+                    torch.from_numpy(sc).view(torch.int16).to(DEV),
+                    None if b is None else b.to(DEV))
+    return y.float().cpu(), ref
+
+
+@pytest.mark.parametrize("M,K,N,bias", [
+    (1, 128, 128, False), (16, 256, 256, True), (17, 1024, 128, False), (64, 512, 384, True),
+    (100, 1024, 256, False), (128, 256, 128, False), (129, 1024, 512, True),
+    (300, 2048, 1024, False), (1000, 1024, 6144, False), (777, 3072, 1024, True)])
+def test_awq_gemm_matches_fp32(M, K, N, bias):
+    # Tolerance: fp32 accumulation order and one bf16 rounding of the output.
+    y, ref = _gemm_case(M, K, N, bias, seed=M + K + N)
+    err = (y - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert err <= 1e-2 * scale + 1e-3, (err, scale)
+    cos = torch.nn.functional.cosine_similarity(y, ref, dim=1)
+    assert cos.min().item() > 0.9999
+
+
+def test_awq_gemm_rejects_bad_shapes():
+    x = torch.zeros(4, 100, dtype=torch.bfloat16, device=DEV)
+    qw = torch.zeros(100 // 8, 128, dtype=torch.int32, device=DEV)
+    with pytest.raises(_C.MesError):
+        _C.awq_gemm(x, qw, torch.zeros(1, 16, dtype=torch.int32, device=DEV),
+                    torch.zeros(1, 128, dtype=torch.int16, device=DEV))
+
+
+# ------------------------------------------------------------------------------ norms
+@pytest.mark.parametrize("rows,H", [(1, 1024), (37, 1024), (513, 1536), (64, 4096)])
+def test_rmsnorm_and_add_rmsnorm(rows, H):
+    g = torch.Generator().manual_seed(rows + H)
+    x = bf16(torch.randn(rows, H, generator=g))
+    r = bf16(torch.randn(rows, H, generator=g))
+    w = bf16(1 + 0.1 * torch.randn(H, generator=g))
+    # Tolerance: the kernel's fp32 rsqrt may move the first of the two bf16 roundings
+    # (normalised value, then * weight) by one step -> at most 2 ulps.
+    want = ops.rms_norm(x, w, 1e-6)
+    got = _C.rmsnorm(x.to(DEV), w.to(DEV), 1e-6).cpu()
+    assert ulp_close(got, want, 2)
+    wy, wr = ops.add_rms_norm(x, r, w, 1e-6)
+    xd, rd = x.to(DEV), r.to(DEV)
+    gy, gr = _C.add_rmsnorm(xd, rd, w.to(DEV), 1e-6)
+    assert torch.equal(gr.cpu(), wr)            # residual: one rounding of an exact fp32 sum
+    assert ulp_close(gy.cpu(), wy, 2)
+    # in place (the model's use): y -> x, residual_out -> residual
+    _C.add_rmsnorm(xd, rd, w.to(DEV), 1e-6, out=xd, residual_out=rd)
+    assert torch.equal(rd.cpu(), wr) and ulp_close(xd.cpu(), wy, 2)
+
+
+# ------------------------------------------------------------------------------ rope
+@pytest.mark.parametrize("norm,f32cache", [(True, False), (False, False), (True, True)])
+def test_qknorm_rope(norm, f32cache):
+    T, Hq, Hkv, D = 300, 16, 8, 128
+    g = torch.Generator().manual_seed(3)
+    qkv = bf16(torch.randn(T, (Hq + 2 * Hkv) * D, generator=g))
+    positions = torch.cat([torch.arange(100), torch.arange(150), torch.arange(50) + 4000])
+    cache = ops.rope_cos_sin_cache(D, 8192, 1e6)
+    cache = cache if f32cache else bf16(cache)
+    qw = bf16(1 + 0.1 * torch.randn(D, generator=g))
+    kw = bf16(1 + 0.1 * torch.randn(D, generator=g))
+    q, k, v = qkv.split([Hq * D, Hkv * D, Hkv * D], dim=1)
+    if norm:
+        q = ops.rms_norm(q.reshape(T, Hq, D), qw, 1e-6).reshape(T, -1)
+        k = ops.rms_norm(k.reshape(T, Hkv, D), kw, 1e-6).reshape(T, -1)
+    want_q = ops.apply_rope(q, positions, cache, D)
+    want_k = ops.apply_rope(k, positions, cache, D)
+    d = qkv.to(DEV)
+    _C.qknorm_rope(d, positions.to(DEV), cache.to(DEV), Hq, Hkv, D,
+                   qw.to(DEV) if norm else None, kw.to(DEV) if norm else None)
+    got = d.cpu()
+    if norm:
+        # The normalised head may differ by 2 ulps (see test_rmsnorm_and_add_rmsnorm); the
+        # rotation mixes two such values, so compare with an absolute bound of 2-4 ulps of
+        # the largest input magnitude.
+        tol = 4 * 2.0 ** -8 * float(max(want_q.abs().max(), want_k.abs().max()))
+        assert (got[:, :Hq * D].float() - want_q.float()).abs().max() <= tol
+        assert (got[:, Hq * D:(Hq + Hkv) * D].float() - want_k.float()).abs().max() <= tol
+    else:
+        assert ulp_close(got[:, :Hq * D], want_q, 1)
+        assert ulp_close(got[:, Hq * D:(Hq + Hkv) * D], want_k, 1)
+    assert torch.equal(got[:, (Hq + Hkv) * D:], v)
+
+
+# ------------------------------------------------------------------------------ misc
+def test_silu_mul():
+    g = torch.Generator().manual_seed(5)
+    x = bf16(torch.randn(333, 2 * 3072, generator=g) * 3)
+    want = bf16(ops.silu_and_mul(x.float()))
+    got = _C.silu_mul(x.to(DEV)).cpu()
+    assert ulp_close(got, want, 1)
+
+
+def test_embedding_exact():
+    g = torch.Generator().manual_seed(6)
+    table = bf16(torch.randn(1000, 1024, generator=g))
+    ids = torch.randint(0, 1000, (777,), generator=g)
+    got = _C.embedding(ids.to(DEV), table.to(DEV)).cpu()
+    assert torch.equal(got, ops.embedding(ids, table))
+    assert _C.take_device_error() == 0
+
+
+def test_last_token_l2():
+    g = torch.Generator().manual_seed(8)
+    hidden = bf16(torch.randn(500, 1024, generator=g))
+    idx = torch.tensor([0, 99, 100, 499])
+    got = _C.last_token_l2(hidden.to(DEV), idx.to(DEV)).cpu()
+    want = ops.last_token_l2(hidden, idx)
+    assert torch.allclose(got, want, atol=1e-6, rtol=1e-5)
+
+
+@pytest.mark.parametrize("lengths", [[1], [5, 1, 1, 7], [128, 129, 127, 1000, 3],
+                                     [4096, 64, 1]])
+def test_varlen_schedule_cu_seqlens(lengths):
+    _, pos, _ = synthetic.packed_batch(lengths, 100)
+    positions = torch.from_numpy(pos)
+    ws = _C.varlen_schedule(positions.to(DEV))
+    cu, n = _C.varlen_cu_seqlens(ws, len(pos))
+    n = int(n.item())
+    want = ops.cu_seqlens_from_positions(positions)
+    assert n == len(want) - 1
+    assert torch.equal(cu[: n + 1].cpu().to(torch.int64), want)
+
+
+# ------------------------------------------------------------------------------ attention
+@pytest.mark.parametrize("lengths,Hq,Hkv", [
+    ([1], 2, 1), ([5, 1, 127, 128, 129], 16, 8), ([300, 1000], 12, 2), ([257, 64, 700], 4, 4)])
+def test_varlen_attention(lengths, Hq, Hkv):
+    D = 128
+    _, pos, _ = synthetic.packed_batch(lengths, 100)
+    positions = torch.from_numpy(pos)
+    T = len(pos)
+    g = torch.Generator().manual_seed(T + Hq)
+    qkv = bf16(torch.randn(T, (Hq + 2 * Hkv) * D, generator=g))
+    q, k, v = qkv.split([Hq * D, Hkv * D, Hkv * D], dim=1)
+    cu = ops.cu_seqlens_from_positions(positions)
+    want = ops.varlen_causal_attention(q.float(), k.float(), v.float(), cu, Hq, Hkv, D)
+    ws = _C.varlen_schedule(positions.to(DEV))
+    got = _C.varlen_attention(qkv.to(DEV), ws, Hq, Hkv, D, D ** -0.5).float().cpu()
+    assert _C.take_device_error() == 0
+    err = (got - want).abs().max().item()
+    assert err < 2e-2, err
