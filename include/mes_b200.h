@@ -54,6 +54,11 @@ int mes_take_device_error(int* code);
 int mes_embedding(const int64_t* ids, int64_t T, const void* table, int64_t vocab,
                   int64_t H, void* out, void* stream);
 
+/* Same gather widened exactly to f32 [T, H]: the start of the model's fp32 residual stream
+ * (the reference keeps the residual in bf16: models/qwen3.py:131-133). */
+int mes_embedding_f32(const int64_t* ids, int64_t T, const void* table, int64_t vocab,
+                      int64_t H, float* out, void* stream);
+
 /* ---------------------------------------------------------------------------------
  * RMSNorm.  y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w), statistics in fp32.
  * Replaces RMSNorm.rms_forward (layers/layernorm.py:18-27).
@@ -61,6 +66,10 @@ int mes_embedding(const int64_t* ids, int64_t T, const void* table, int64_t voca
  * ------------------------------------------------------------------------------- */
 int mes_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t H, float eps,
                 void* stream);
+
+/* RMSNorm of an f32 input (the fp32 residual stream) to bf16 y; same arithmetic. */
+int mes_rmsnorm_f32in(const float* x, const void* w, void* y, int64_t rows, int64_t H,
+                      float eps, void* stream);
 
 /* ---------------------------------------------------------------------------------
  * Fused residual add + RMSNorm.  s = x + residual (fp32); residual_out = bf16(s);
@@ -71,6 +80,12 @@ int mes_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t H, 
  * ------------------------------------------------------------------------------- */
 int mes_add_rmsnorm(const void* x, const void* residual, const void* w, void* y,
                     void* residual_out, int64_t rows, int64_t H, float eps, void* stream);
+
+/* Fused add + RMSNorm with a f32 residual stream: s = x + residual (x bf16 [rows, H],
+ * residual f32 [rows, H] updated in place to s), y = bf16 RMSNorm(s) as above.  Used after
+ * the tensor-parallel all-reduce of the o_proj / down_proj partial sums. */
+int mes_add_rmsnorm_f32res(const void* x, float* residual, const void* w, void* y,
+                           int64_t rows, int64_t H, float eps, void* stream);
 
 /* ---------------------------------------------------------------------------------
  * Fused per-head q/k RMSNorm + NeoX RoPE, in place on the packed QKV projection output.
@@ -163,6 +178,15 @@ int mes_awq_dequant(const int32_t* qweight_mes, const int32_t* qzeros, const voi
 int mes_awq_gemm(const void* X, int64_t ldx, const int32_t* qweight_mes,
                  const int32_t* qzeros, const void* scales, const void* bias, void* Y,
                  int64_t ldy, int64_t M, int64_t N, int64_t K, int group_size, void* stream);
+
+/* Same product accumulated into a f32 residual stream: R[M, N] += X * W (+ bias), pitch ldr
+ * elements.  This is RowParallelLinear.forward (layers/linear.py:176-180) at tp == 1 fused
+ * with the residual add of the following RMSNorm.add_rms_forward (layers/layernorm.py:36),
+ * without rounding the projection output to bf16 first. */
+int mes_awq_gemm_residual(const void* X, int64_t ldx, const int32_t* qweight_mes,
+                          const int32_t* qzeros, const void* scales, const void* bias, float* R,
+                          int64_t ldr, int64_t M, int64_t N, int64_t K, int group_size,
+                          void* stream);
 
 #ifdef __cplusplus
 }

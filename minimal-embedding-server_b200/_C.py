@@ -23,8 +23,11 @@ SIGNATURES = {
     "mes_status_string": (ctypes.c_char_p, [_i32]),
     "mes_take_device_error": (_i32, [ctypes.POINTER(_i32)]),
     "mes_embedding": (_i32, [_vp, _i64, _vp, _i64, _i64, _vp, _vp]),
+    "mes_embedding_f32": (_i32, [_vp, _i64, _vp, _i64, _i64, _vp, _vp]),
     "mes_rmsnorm": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _vp]),
+    "mes_rmsnorm_f32in": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _vp]),
     "mes_add_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
+    "mes_add_rmsnorm_f32res": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
     "mes_qknorm_rope": (_i32, [_vp, _i64, _vp, _vp, _i32, _i64, _vp, _vp, _i64, _i32, _i32,
                                _i32, _f32, _i32, _vp]),
     "mes_silu_mul": (_i32, [_vp, _vp, _i64, _i64, _vp]),
@@ -37,6 +40,8 @@ SIGNATURES = {
     "mes_awq_dequant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp]),
     "mes_awq_gemm": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32,
                             _vp]),
+    "mes_awq_gemm_residual": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                                     _i32, _vp]),
 }
 
 _lib = None
@@ -117,12 +122,41 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None =
     return out
 
 
+def embedding_f32(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None):
+    """Gather widened to fp32 (the start of the fp32 residual stream)."""
+    _need(ids.dtype == torch.int64 and ids.dim() == 1, "ids must be int64 [T]")
+    _need(table.dtype == torch.bfloat16 and table.dim() == 2 and table.is_contiguous(),
+          "table must be contiguous bf16 [vocab, H]")
+    T, (V, H) = ids.shape[0], table.shape
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.float32, device=table.device)
+    _check(lib().mes_embedding_f32(_p(ids.contiguous()), T, _p(table), V, H, _p(out),
+                                   _stream(table)), "mes_embedding_f32")
+    return out
+
+
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None):
-    _need(x.dtype == torch.bfloat16 and x.is_contiguous(), "x must be contiguous bf16")
+    """bf16 RMSNorm of a bf16 or fp32 ``x`` (fp32: the residual stream)."""
+    _need(x.dtype in (torch.bfloat16, torch.float32) and x.is_contiguous(),
+          "x must be contiguous bf16 or fp32")
+    H = x.shape[-1]
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    fn = lib().mes_rmsnorm if x.dtype == torch.bfloat16 else lib().mes_rmsnorm_f32in
+    _check(fn(_p(x), _p(w), _p(out), x.numel() // H, H, eps, _stream(x)), "mes_rmsnorm")
+    return out
+
+
+def add_rmsnorm_f32res(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """residual (fp32, in place) += x (bf16); returns bf16 RMSNorm(residual)."""
+    _need(x.dtype == torch.bfloat16 and residual.dtype == torch.float32, "bf16 x, fp32 residual")
+    _need(x.is_contiguous() and residual.is_contiguous() and x.shape == residual.shape,
+          "x and residual must be contiguous and of one shape")
     H = x.shape[-1]
     out = torch.empty_like(x) if out is None else out
-    _check(lib().mes_rmsnorm(_p(x), _p(w), _p(out), x.numel() // H, H, eps, _stream(x)),
-           "mes_rmsnorm")
+    _check(lib().mes_add_rmsnorm_f32res(_p(x), _p(residual), _p(w), _p(out), x.numel() // H, H,
+                                        eps, _stream(x)), "mes_add_rmsnorm_f32res")
     return out
 
 
@@ -239,6 +273,29 @@ def awq_dequant(qweight_mes: torch.Tensor, qzeros: torch.Tensor, scales: torch.T
     _check(lib().mes_awq_dequant(_p(qweight_mes), _p(qzeros), _p(scales), K, N, group_size,
                                  _p(out), _stream(qweight_mes)), "mes_awq_dequant")
     return out
+
+
+def awq_gemm_residual(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
+                      scales: torch.Tensor, residual: torch.Tensor,
+                      bias: torch.Tensor | None = None, group_size: int = 128) -> torch.Tensor:
+    """``residual[M, N] (fp32) += x @ W (+ bias)`` in the GEMM epilogue."""
+    _need(x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(-1) == 1,
+          "x must be bf16 [M, K] with unit inner stride")
+    _need(residual.dtype == torch.float32 and residual.stride(-1) == 1, "fp32 residual")
+    K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
+    M = x.shape[0]
+    _need(x.shape[1] == K and tuple(residual.shape) == (M, N), "shape mismatch")
+    ev = gemm_events
+    if ev is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+    _check(lib().mes_awq_gemm_residual(_p(x), x.stride(0), _p(qweight_mes), _p(qzeros),
+                                       _p(scales), _p(bias), _p(residual), residual.stride(0),
+                                       M, N, K, group_size, _stream(x)), "mes_awq_gemm_residual")
+    if ev is not None:
+        e1.record()
+        ev.append((e0, e1, 2.0 * M * N * K))
+    return residual
 
 
 def awq_gemm(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,

@@ -83,6 +83,7 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
   }
   if (warp == 0 && lane == 0) mes::tma_prefetch_desc(&map_qkv);
   if (warp == 1) {
+    __syncwarp();
     mes::tmem_alloc(tmem_slot, kTmemCols);
     mes::tmem_relinquish();
   }
@@ -134,6 +135,7 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
         }
       }
     }
+    __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------ MMA ----------------------------------------
     if (lane == 0) {
@@ -188,6 +190,7 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
         }
       }
     }
+    __syncwarp();
   } else {
     // ---------------------------------- softmax -------------------------------------
     const int q = warp & 3;
@@ -203,7 +206,7 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
       float m = -INFINITY, l = 0.f;
       for (int i = 0; i < nt; ++i) {
         const int t = it + i, sb = t & 1;
-        if (!mes::mbar_wait(&s_full[sb], (t >> 1) & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
+        if (!mes::mbar_wait_warp(&s_full[sb], (t >> 1) & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
         mes::tc_fence_after();
         float s[kTile];
 #pragma unroll
@@ -217,6 +220,7 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
         mes::tc_fence_before();
         __syncwarp();
         if (lane == 0) mes::mbar_arrive(&s_free[sb]);
+        __syncwarp();
         // Causal mask on the diagonal tile: key c is visible to row r iff c <= r.
         if (i == nt - 1) {
 #pragma unroll
@@ -228,14 +232,17 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
         for (int c = 0; c < kTile; ++c) mx = fmaxf(mx, s[c]);
         mx *= scale_log2;
         // PV_{i-1} must be done before O is rescaled or P overwritten.
-        if (i > 0 && !mes::mbar_wait(pv_done, (t - 1) & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
+        if (i > 0 && !mes::mbar_wait_warp(pv_done, (t - 1) & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
         mes::tc_fence_after();
         if (i == 0) {
           m = mx;
-        } else if (mx > m + 8.0f) {
-          const float f = exp2f(m - mx);
+        } else if (__any_sync(0xffffffffu, mx > m + 8.0f)) {
+          // Warp-uniform decision (tcgen05.ld/st are warp-collective): every row of the
+          // warp moves to max(m, mx); rows whose maximum did not grow scale by 1.
+          const float mn = fmaxf(m, mx);
+          const float f = exp2f(m - mn);
           l *= f;
-          m = mx;
+          m = mn;
 #pragma unroll 1
           for (int c = 0; c < kD; c += 32) {
             uint32_t v[32];
@@ -269,11 +276,12 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
         mes::tc_fence_before();
         __syncwarp();
         if (lane == 0) mes::mbar_arrive(p_full);
+        __syncwarp();
       }
       if (!ok) break;
       // Epilogue: O / l for this item's rows.
       const int tl = it + nt - 1;
-      if (!mes::mbar_wait(pv_done, tl & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
+      if (!mes::mbar_wait_warp(pv_done, tl & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
       mes::tc_fence_after();
       const int row_in_seq = item.y * kTile + r;
       const bool valid = row_in_seq < len;
@@ -304,6 +312,7 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
   mes::tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();
     mes::tc_fence_after();
     mes::tmem_dealloc(tmem, kTmemCols);
   }

@@ -96,12 +96,15 @@ struct Cfg {
   static_assert(kXStage % 1024 == 0, "swizzle atoms");
 };
 
-template <int BT, int STAGES>
+// kResidual: instead of storing bf16 Y, the epilogue accumulates into a fp32 residual
+// stream, R[t, n] += acc + bias (the residual add of the decoder block fused into the
+// o_proj / down_proj GEMM).
+template <int BT, int STAGES, bool kResidual>
 __global__ void __launch_bounds__(kThreads)
 awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                 const __grid_constant__ CUtensorMap map_y, const int32_t* __restrict__ qzeros,
                 const uint16_t* __restrict__ scales, const __nv_bfloat16* __restrict__ bias,
-                int M, int N, int K) {
+                float* __restrict__ R, int64_t ldr, int M, int N, int K) {
   using C = Cfg<BT, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -138,6 +141,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
     mes::tma_prefetch_desc(&map_y);
   }
   if (warp == 1) {
+    __syncwarp();
     mes::tmem_alloc(tmem_slot, C::kTmemCols);
     mes::tmem_relinquish();
   }
@@ -171,6 +175,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
         }
       }
     }
+    __syncwarp();
   } else if (warp == 1) {
     // ------------------------------- MMA issuer ---------------------------------------
     if (lane == 0) {
@@ -197,6 +202,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
         }
       }
     }
+    __syncwarp();
   } else {
     // --------------------------- dequant + epilogue warps -----------------------------
     const int q = warp & 3;                 // TMEM lane quadrant of this warp
@@ -221,7 +227,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
           sraw = __ldg(scales + (int64_t)gn * N + n);
         }
       }
-      if (!mes::mbar_wait(&full[s], ph, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) { ok = false; break; }
+      if (!mes::mbar_wait_warp(&full[s], ph, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) { ok = false; break; }
       mes::tc_fence_after();
       const uint32_t* wsrc = ws + s * (C::kWStage / 4) + row;
       uint32_t a[32];
@@ -238,8 +244,9 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
       mes::tc_fence_before();
       __syncwarp();
       if (lane == 0) mes::mbar_arrive(&afull[s]);
+      __syncwarp();
     }
-    if (ok && mes::mbar_wait(accum, 0, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
+    if (ok && mes::mbar_wait_warp(accum, 0, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
       mes::tc_fence_after();
       const float b = bias ? __bfloat162float(bias[n]) : 0.f;
       __nv_bfloat16* mybuf = outbuf + (warp - 2) * 2 * 32 * 32;
@@ -250,19 +257,32 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
         else mes::tmem_ld16(tmem + lane_off + c0, v);
         mes::tmem_wait_ld();
         if (t0 + c0 >= M) break;  // rows past the end of X: nothing to store
-        __nv_bfloat16* buf = mybuf + ((c0 / C::kChunk) & 1) * 32 * 32;
-        if (c0 >= 2 * C::kChunk) {
-          if (lane == 0) mes::tma_store_wait_read<1>();
-          __syncwarp();
-        }
+        if constexpr (kResidual) {
+          // Each lane owns feature n; a warp touches 32 consecutive fp32 per token row.
+          const int rows = min(C::kChunk, M - (t0 + c0));
+          float* rp = R + (int64_t)(t0 + c0) * ldr + n;
+          float rv[C::kChunk];
 #pragma unroll
-        for (int j = 0; j < C::kChunk; ++j)
-          buf[j * 32 + lane] = __float2bfloat16_rn(__uint_as_float(v[j]) + b);
-        mes::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          mes::tma_store_2d(&map_y, buf, n0 + q * 32, t0 + c0);
-          mes::tma_store_commit();
+          for (int j = 0; j < C::kChunk; ++j) rv[j] = j < rows ? rp[(int64_t)j * ldr] : 0.f;
+#pragma unroll
+          for (int j = 0; j < C::kChunk; ++j)
+            if (j < rows) rp[(int64_t)j * ldr] = rv[j] + (__uint_as_float(v[j]) + b);
+        } else {
+          __nv_bfloat16* buf = mybuf + ((c0 / C::kChunk) & 1) * 32 * 32;
+          if (c0 >= 2 * C::kChunk) {
+            if (lane == 0) mes::tma_store_wait_read<1>();
+            __syncwarp();
+          }
+#pragma unroll
+          for (int j = 0; j < C::kChunk; ++j)
+            buf[j * 32 + lane] = __float2bfloat16_rn(__uint_as_float(v[j]) + b);
+          mes::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mes::tma_store_2d(&map_y, buf, n0 + q * 32, t0 + c0);
+            mes::tma_store_commit();
+          }
+          __syncwarp();
         }
       }
       if (lane == 0) mes::tma_store_wait_all<0>();
@@ -273,6 +293,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
   mes::tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();
     mes::tc_fence_after();
     mes::tmem_dealloc(tmem, C::kTmemCols);
   }
@@ -320,26 +341,53 @@ __global__ void awq_dequant_kernel(const uint32_t* __restrict__ qw, const int32_
   }
 }
 
-template <int BT, int STAGES>
+template <int BT, int STAGES, bool kResidual>
 int launch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
                 const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
                 int64_t N, int64_t K, cudaStream_t stream) {
   using C = Cfg<BT, STAGES>;
-  cudaError_t e = cudaFuncSetAttribute(awq_gemm_kernel<BT, STAGES>,
+  cudaError_t e = cudaFuncSetAttribute(awq_gemm_kernel<BT, STAGES, kResidual>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   if (e != cudaSuccess) return MES_ERR_CUDA;
   CUtensorMap mx, mw, my;
   if (!mes_host::make_map_2d(&mx, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, ldx, BT, kBK,
                              CU_TENSOR_MAP_SWIZZLE_128B) ||
       !mes_host::make_map_2d(&mw, qw, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, K / 8, N, N, kBK / 8, kBN,
-                             CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !mes_host::make_map_2d(&my, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, N, ldy, C::kChunk, 32,
                              CU_TENSOR_MAP_SWIZZLE_NONE))
     return MES_ERR_INVALID;
+  if (kResidual) {
+    my = mx;  // unused by the residual epilogue
+  } else if (!mes_host::make_map_2d(&my, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, N, ldy,
+                                    C::kChunk, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+    return MES_ERR_INVALID;
+  }
   dim3 grid((unsigned)(N / kBN), (unsigned)((M + BT - 1) / BT));
-  awq_gemm_kernel<BT, STAGES><<<grid, kThreads, C::kSmem, stream>>>(
-      mx, mw, my, qzeros, (const uint16_t*)scales, (const __nv_bfloat16*)bias, (int)M, (int)N, (int)K);
+  awq_gemm_kernel<BT, STAGES, kResidual><<<grid, kThreads, C::kSmem, stream>>>(
+      mx, mw, my, qzeros, (const uint16_t*)scales, (const __nv_bfloat16*)bias,
+      kResidual ? (float*)Y : nullptr, ldy, (int)M, (int)N, (int)K);
   return mes_host::from_cuda(cudaGetLastError());
+}
+
+template <bool kResidual>
+int dispatch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
+                  const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
+                  int64_t N, int64_t K, cudaStream_t s) {
+  if (M <= 16) return launch_gemm<16, 6, kResidual>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  if (M <= 32) return launch_gemm<32, 6, kResidual>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  if (M <= 64) return launch_gemm<64, 6, kResidual>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  return launch_gemm<128, 4, kResidual>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+}
+
+int check_gemm_args(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
+                    const void* scales, const void* Y, int64_t ldy, int64_t M, int64_t N,
+                    int64_t K, int group_size, int y_elem_align) {
+  if (M < 0 || N <= 0 || K <= 0 || N % kBN || K % kGroup || group_size != kGroup)
+    return MES_ERR_INVALID;
+  if (N > (1 << 30) || K > (1 << 30) || M > (1LL << 31) - 256) return MES_ERR_INVALID;
+  if (ldx < K || ldy < N || ldx % 8 || ldy % y_elem_align) return MES_ERR_INVALID;
+  if (M == 0) return -1;
+  if (!X || !qw || !qzeros || !scales || !Y) return MES_ERR_INVALID;
+  return MES_OK;
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -383,16 +431,23 @@ extern "C" int mes_awq_gemm(const void* X, int64_t ldx, const int32_t* qweight_m
                             const int32_t* qzeros, const void* scales, const void* bias, void* Y,
                             int64_t ldy, int64_t M, int64_t N, int64_t K, int group_size,
                             void* stream) {
-  if (M < 0 || N <= 0 || K <= 0 || N % kBN || K % kGroup || group_size != kGroup)
-    return MES_ERR_INVALID;
-  if (N > (1 << 30) || K > (1 << 30) || M > (1LL << 31) - 256) return MES_ERR_INVALID;
-  if (ldx < K || ldy < N || ldx % 8 || ldy % 8) return MES_ERR_INVALID;
-  if (M == 0) return MES_OK;
-  if (!X || !qweight_mes || !qzeros || !scales || !Y) return MES_ERR_INVALID;
+  const int st = check_gemm_args(X, ldx, qweight_mes, qzeros, scales, Y, ldy, M, N, K,
+                                 group_size, 8);
+  if (st != MES_OK) return st < 0 ? MES_OK : st;
   if (!aligned16(X) || !aligned16(Y) || !aligned16(qweight_mes)) return MES_ERR_ALIGN;
-  cudaStream_t s = (cudaStream_t)stream;
-  if (M <= 16) return launch_gemm<16, 6>(X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K, s);
-  if (M <= 32) return launch_gemm<32, 6>(X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K, s);
-  if (M <= 64) return launch_gemm<64, 6>(X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K, s);
-  return launch_gemm<128, 4>(X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  return dispatch_gemm<false>(X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K,
+                              (cudaStream_t)stream);
+}
+
+extern "C" int mes_awq_gemm_residual(const void* X, int64_t ldx, const int32_t* qweight_mes,
+                                     const int32_t* qzeros, const void* scales, const void* bias,
+                                     float* R, int64_t ldr, int64_t M, int64_t N, int64_t K,
+                                     int group_size, void* stream) {
+  const int st = check_gemm_args(X, ldx, qweight_mes, qzeros, scales, R, ldr, M, N, K,
+                                 group_size, 1);
+  if (st != MES_OK) return st < 0 ? MES_OK : st;
+  if (!aligned16(X) || !aligned16(qweight_mes) || (reinterpret_cast<uintptr_t>(R) & 3))
+    return MES_ERR_ALIGN;
+  return dispatch_gemm<true>(X, ldx, qweight_mes, qzeros, scales, bias, R, ldr, M, N, K,
+                             (cudaStream_t)stream);
 }

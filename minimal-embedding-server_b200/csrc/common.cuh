@@ -82,6 +82,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// Warp-wide bounded wait: every lane waits, then the warp reconverges and agrees on the
+// result, so the tcgen05 ".sync.aligned" instructions that follow run converged.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
+                                               volatile int* abort_flag, int* err, int code) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, err, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ------------------------------------- TMA ----------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

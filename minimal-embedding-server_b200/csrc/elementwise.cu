@@ -28,6 +28,22 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   for (int i = 0; i < 4; ++i) u[i] = mes::pack_bf16x2(f[2 * i], f[2 * i + 1]);
   return v;
 }
+// 8 consecutive elements of a bf16 or fp32 row as fp32 registers.
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  unpack8(*reinterpret_cast<const uint4*>(p), f);
+}
+__device__ __forceinline__ void load8(const float* p, float (&f)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
+  *reinterpret_cast<uint4*>(p) = pack8(f);
+}
+__device__ __forceinline__ void store8(float* p, const float (&f)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+}
+
 // Round fp32 to bf16 and back (the reference's `.to(orig_dtype)` before `* weight`).
 __device__ __forceinline__ float round_bf16(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
@@ -52,40 +68,46 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // ------------------------------------ embedding ----------------------------------------
+// out[t] = table[ids[t]] as bf16 (copy) or fp32 (exact widening, to start a fp32 residual).
+template <typename OT>
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, int64_t T,
-                                 const uint4* __restrict__ table, int64_t vocab, int64_t hv,
-                                 uint4* __restrict__ out) {
+                                 const __nv_bfloat16* __restrict__ table, int64_t vocab, int64_t hv,
+                                 OT* __restrict__ out) {
   const int64_t total = T * hv;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t t = i / hv, c = i - t * hv;
     const int64_t id = __ldg(ids + t);
-    uint4 v = make_uint4(0, 0, 0, 0);
+    float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (id >= 0 && id < vocab) {
-      v = __ldg(table + id * hv + c);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(table + (id * hv + c) * 8)), f);
     } else if (c == 0) {
       atomicCAS(&g_err_elementwise, 0, MES_ERR_INVALID);
     }
-    out[i] = v;
+    store8(out + i * 8, f);
   }
 }
 
 // ------------------------------------- RMSNorm -----------------------------------------
-// One block per row, one 8-element vector per thread (blockDim.x = H / 8).
-template <bool kAdd>
-__global__ void rmsnorm_kernel(const uint4* x, const uint4* residual, const uint4* __restrict__ w,
-                               uint4* y, uint4* residual_out, int hv, float inv_h, float eps) {
+// One block per row, one 8-element vector per thread (blockDim.x = H / 8).  XT is the
+// input type, RT the residual type (bf16: the reference's layout; fp32: the model's
+// residual stream).  With kAdd, s = x + residual is formed in fp32, stored to
+// residual_out (rounded to RT) and normalised; y = bf16(bf16(s * rsqrt(mean + eps)) * w).
+template <typename XT, typename RT, bool kAdd>
+__global__ void rmsnorm_kernel(const XT* x, const RT* residual, const uint4* __restrict__ w,
+                               __nv_bfloat16* y, RT* residual_out, int hv, float inv_h, float eps) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int c = threadIdx.x;
+  const int64_t off = (row * hv + c) * 8;
   float f[8];
-  unpack8(x[row * hv + c], f);
+  load8(x + off, f);
   if (kAdd) {
     float r[8];
-    unpack8(residual[row * hv + c], r);
+    load8(residual + off, r);
 #pragma unroll
     for (int i = 0; i < 8; ++i) f[i] += r[i];
-    residual_out[row * hv + c] = pack8(f);  // new residual = bf16(x + r)
+    store8(residual_out + off, f);
   }
   float ss = 0.f;
 #pragma unroll
@@ -96,7 +118,7 @@ __global__ void rmsnorm_kernel(const uint4* x, const uint4* residual, const uint
   unpack8(w[c], wf);
 #pragma unroll
   for (int i = 0; i < 8; ++i) f[i] = round_bf16(f[i] * rs) * wf[i];
-  y[row * hv + c] = pack8(f);
+  store8(y + off, f);
 }
 
 // ------------------------------ q/k RMSNorm + NeoX RoPE --------------------------------
@@ -318,47 +340,72 @@ extern "C" int mes_elementwise_take_error(int* code) {
   return mes_host::from_cuda(e);
 }
 
-extern "C" int mes_embedding(const int64_t* ids, int64_t T, const void* table, int64_t vocab,
-                             int64_t H, void* out, void* stream) {
+static int launch_embedding(bool f32, const int64_t* ids, int64_t T, const void* table,
+                            int64_t vocab, int64_t H, void* out, void* stream) {
   if (T < 0 || vocab <= 0 || H <= 0 || H % 8) return MES_ERR_INVALID;
   if (T == 0) return MES_OK;
   if (!ids || !table || !out) return MES_ERR_INVALID;
   if (!aligned16(table) || !aligned16(out)) return MES_ERR_ALIGN;
   const int64_t hv = H / 8;
-  embedding_kernel<<<grid_for(T * hv, 256), 256, 0, (cudaStream_t)stream>>>(
-      ids, T, (const uint4*)table, vocab, hv, (uint4*)out);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (f32)
+    embedding_kernel<float><<<grid_for(T * hv, 256), 256, 0, s>>>(
+        ids, T, (const __nv_bfloat16*)table, vocab, hv, (float*)out);
+  else
+    embedding_kernel<__nv_bfloat16><<<grid_for(T * hv, 256), 256, 0, s>>>(
+        ids, T, (const __nv_bfloat16*)table, vocab, hv, (__nv_bfloat16*)out);
   return mes_host::from_cuda(cudaGetLastError());
 }
 
-static int launch_rmsnorm(bool add, const void* x, const void* residual, const void* w, void* y,
+extern "C" int mes_embedding(const int64_t* ids, int64_t T, const void* table, int64_t vocab,
+                             int64_t H, void* out, void* stream) {
+  return launch_embedding(false, ids, T, table, vocab, H, out, stream);
+}
+
+extern "C" int mes_embedding_f32(const int64_t* ids, int64_t T, const void* table, int64_t vocab,
+                                 int64_t H, float* out, void* stream) {
+  return launch_embedding(true, ids, T, table, vocab, H, out, stream);
+}
+
+template <typename XT, typename RT, bool kAdd>
+static int launch_rmsnorm(const void* x, const void* residual, const void* w, void* y,
                           void* residual_out, int64_t rows, int64_t H, float eps, void* stream) {
   if (rows < 0 || H <= 0 || H % 256 || H / 8 > 1024) return MES_ERR_INVALID;
   if (rows == 0) return MES_OK;
-  if (!x || !w || !y || (add && (!residual || !residual_out))) return MES_ERR_INVALID;
+  if (!x || !w || !y || (kAdd && (!residual || !residual_out))) return MES_ERR_INVALID;
   if (!aligned16(x) || !aligned16(w) || !aligned16(y) ||
-      (add && (!aligned16(residual) || !aligned16(residual_out))))
+      (kAdd && (!aligned16(residual) || !aligned16(residual_out))))
     return MES_ERR_ALIGN;
   if (rows > 0x7fffffffLL) return MES_ERR_INVALID;
   const int hv = (int)(H / 8);
-  if (add)
-    rmsnorm_kernel<true><<<(unsigned)rows, hv, 0, (cudaStream_t)stream>>>(
-        (const uint4*)x, (const uint4*)residual, (const uint4*)w, (uint4*)y, (uint4*)residual_out,
-        hv, 1.0f / (float)H, eps);
-  else
-    rmsnorm_kernel<false><<<(unsigned)rows, hv, 0, (cudaStream_t)stream>>>(
-        (const uint4*)x, nullptr, (const uint4*)w, (uint4*)y, nullptr, hv, 1.0f / (float)H, eps);
+  rmsnorm_kernel<XT, RT, kAdd><<<(unsigned)rows, hv, 0, (cudaStream_t)stream>>>(
+      (const XT*)x, (const RT*)residual, (const uint4*)w, (__nv_bfloat16*)y, (RT*)residual_out, hv,
+      1.0f / (float)H, eps);
   return mes_host::from_cuda(cudaGetLastError());
 }
 
 extern "C" int mes_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t H,
                            float eps, void* stream) {
-  return launch_rmsnorm(false, x, nullptr, w, y, nullptr, rows, H, eps, stream);
+  return launch_rmsnorm<__nv_bfloat16, __nv_bfloat16, false>(x, nullptr, w, y, nullptr, rows, H,
+                                                             eps, stream);
+}
+
+extern "C" int mes_rmsnorm_f32in(const float* x, const void* w, void* y, int64_t rows, int64_t H,
+                                 float eps, void* stream) {
+  return launch_rmsnorm<float, float, false>(x, nullptr, w, y, nullptr, rows, H, eps, stream);
 }
 
 extern "C" int mes_add_rmsnorm(const void* x, const void* residual, const void* w, void* y,
                                void* residual_out, int64_t rows, int64_t H, float eps,
                                void* stream) {
-  return launch_rmsnorm(true, x, residual, w, y, residual_out, rows, H, eps, stream);
+  return launch_rmsnorm<__nv_bfloat16, __nv_bfloat16, true>(x, residual, w, y, residual_out, rows,
+                                                            H, eps, stream);
+}
+
+extern "C" int mes_add_rmsnorm_f32res(const void* x, float* residual, const void* w, void* y,
+                                      int64_t rows, int64_t H, float eps, void* stream) {
+  return launch_rmsnorm<__nv_bfloat16, float, true>(x, residual, w, y, residual, rows, H, eps,
+                                                    stream);
 }
 
 extern "C" int mes_qknorm_rope(void* qkv, int64_t ld, const int64_t* positions,

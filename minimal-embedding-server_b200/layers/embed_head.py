@@ -33,3 +33,7 @@ class VocabParallelEmbedding(nn.Module):
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         return _C.embedding(x, self.weight, out)
+
+    def forward_f32(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """The lookup widened to fp32: the first value of the fp32 residual stream."""
+        return _C.embedding_f32(x, self.weight, out)

@@ -5,6 +5,9 @@ statistics (``rms_forward:18-27``); ``forward(x, residual)`` first forms the fp3
 ``s = x + residual``, returns ``bf16(s)`` as the new residual and normalises ``s``
 (``add_rms_forward:30-41``).  Both run as one fused sm_100a kernel.  Inputs are not
 modified unless the caller passes ``out=`` / ``residual_out=`` buffers that alias them.
+
+``residual_norm`` serves the model's fp32 residual stream: it normalises the fp32
+residual (optionally adding a bf16 delta to it first, in place) and returns bf16.
 """
 from __future__ import annotations
 
@@ -33,6 +36,13 @@ class RMSNorm(nn.Module):
                         out: torch.Tensor | None = None,
                         residual_out: torch.Tensor | None = None):
         return _C.add_rmsnorm(x, residual, self.weight, self.eps, out, residual_out)
+
+    def residual_norm(self, residual: torch.Tensor, delta: torch.Tensor | None = None,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+        """bf16 RMSNorm of the fp32 ``residual`` (after ``residual += delta`` if given)."""
+        if delta is None:
+            return _C.rmsnorm(residual, self.weight, self.eps, out)
+        return _C.add_rmsnorm_f32res(delta, residual, self.weight, self.eps, out)
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None, *,
                 out: torch.Tensor | None = None, residual_out: torch.Tensor | None = None):

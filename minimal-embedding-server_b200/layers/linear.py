@@ -242,3 +242,16 @@ class RowParallelLinear(LinearBase):
         if self.tp_size > 1:
             dist.all_reduce(y)
         return y
+
+    def forward_residual(self, x: torch.Tensor, residual: torch.Tensor) -> torch.Tensor | None:
+        """Add this projection to the fp32 residual stream.  At tp == 1 the add happens in
+        the GEMM epilogue (returns None); at tp > 1 the bf16 partial products are summed
+        with an all-reduce and returned for the following add+RMSNorm to apply."""
+        if self.tp_size > 1:
+            return self.forward(x)
+        if self._qweight_mes is None or self._qweight_mes.device != self.qweight.device:
+            self.process_weights_after_loading()
+        _C.awq_gemm_residual(x.reshape(-1, x.shape[-1]), self._qweight_mes, self.qzeros,
+                             self.scales, residual.view(-1, residual.shape[-1]), self.bias,
+                             group_size=self.group_size)
+        return None

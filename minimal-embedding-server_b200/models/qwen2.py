@@ -3,8 +3,16 @@
 Module tree, parameter names and ``packed_modules_mapping`` match the reference so that
 its checkpoint loader conventions apply.  As in the reference, attention has a QKV bias
 and no q/k norm in ``forward`` (``qwen2.py:81-86``; the norm modules exist, unused), and
-``Qwen2MLP`` (gate_up -> SiLU-and-mul -> down, ``:89-117``) is shared with Qwen3.  The
-residual stream is updated in place by the fused add+RMSNorm kernel.
+``Qwen2MLP`` (gate_up -> SiLU-and-mul -> down, ``:89-117``) is shared with Qwen3.
+
+Residual stream.  The reference keeps the residual in bf16 and rounds every o_proj /
+down_proj output to bf16 before adding it (``layernorm.py:30-41``).  Here the residual is
+fp32 and the projection is accumulated into it inside the GEMM epilogue (tp == 1) or
+after the all-reduce (tp > 1); the block's math is otherwise unchanged.  This removes two
+bf16 roundings per block, which is what keeps full-depth embeddings within the 0.9995
+cosine bound of the fp32 reference.  ``DecoderLayer.forward`` therefore passes
+``(pending_delta, residual_fp32)`` between layers, where ``pending_delta`` is None when
+the projection was already added.
 """
 from __future__ import annotations
 
@@ -70,15 +78,22 @@ class Qwen2Attention(nn.Module):
         self.q_norm = RMSNorm(self.head_dim, eps=rms_norm_eps)
         self.k_norm = RMSNorm(self.head_dim, eps=rms_norm_eps)
 
-    def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor) -> torch.Tensor:
+    def _attend(self, positions: torch.Tensor, hidden_states: torch.Tensor) -> torch.Tensor:
         qkv = self.qkv_proj(hidden_states)
         if self.apply_qk_norm:
             self.rotary_emb.forward_fused(positions, qkv, self.num_heads, self.num_kv_heads,
                                           self.q_norm, self.k_norm)
         else:
             self.rotary_emb.forward_fused(positions, qkv, self.num_heads, self.num_kv_heads)
-        o = self.attn.forward_packed(qkv, positions)
-        return self.o_proj(o)
+        return self.attn.forward_packed(qkv, positions)
+
+    def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor) -> torch.Tensor:
+        """``qwen2.py:76-86`` / ``qwen3.py:76-92``: attention block output (bf16)."""
+        return self.o_proj(self._attend(positions, hidden_states))
+
+    def forward_residual(self, positions, hidden_states, residual):
+        """Attention block added into the fp32 residual stream (see module docstring)."""
+        return self.o_proj.forward_residual(self._attend(positions, hidden_states), residual)
 
 
 class Qwen2MLP(nn.Module):
@@ -97,6 +112,9 @@ class Qwen2MLP(nn.Module):
 
     def forward(self, x):
         return self.down_proj(self.act_fn(self.gate_up_proj(x)))
+
+    def forward_residual(self, x, residual):
+        return self.down_proj.forward_residual(self.act_fn(self.gate_up_proj(x)), residual)
 
 
 def _attn_kwargs(model_config, qkv_bias: bool, qk_norm: bool) -> dict:
@@ -128,19 +146,20 @@ class DecoderLayer(nn.Module):
         self.input_layernorm = RMSNorm(mc.hidden_size, eps=mc.rms_norm_eps)
         self.post_attention_layernorm = RMSNorm(mc.hidden_size, eps=mc.rms_norm_eps)
 
-    def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor,
+    def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor | None,
                 residual: torch.Tensor | None):
+        """One block on the fp32 residual stream.  First layer: ``hidden_states`` is the
+        fp32 embedding, which becomes the residual.  Later layers: ``hidden_states`` is the
+        previous block's pending delta (None once it was added in a GEMM epilogue)."""
         if residual is None:
             residual = hidden_states
-            hidden_states = self.input_layernorm(hidden_states)
+            x = self.input_layernorm.residual_norm(residual)
         else:
-            hidden_states, residual = self.input_layernorm(
-                hidden_states, residual, out=hidden_states, residual_out=residual)
-        hidden_states = self.self_attn(positions, hidden_states)
-        hidden_states, residual = self.post_attention_layernorm(
-            hidden_states, residual, out=hidden_states, residual_out=residual)
-        hidden_states = self.mlp(hidden_states)
-        return hidden_states, residual
+            x = self.input_layernorm.residual_norm(residual, hidden_states)
+        delta = self.self_attn.forward_residual(positions, x, residual)
+        x = self.post_attention_layernorm.residual_norm(residual, delta)
+        delta = self.mlp.forward_residual(x, residual)
+        return delta, residual
 
 
 class Qwen2DecoderLayer(DecoderLayer):
@@ -165,13 +184,11 @@ class DecoderModel(nn.Module):
 
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
         with batch_schedule(positions):
-            hidden_states = self.embed_tokens(input_ids)
+            hidden_states = self.embed_tokens.forward_f32(input_ids)
             residual = None
             for layer in self.layers:
                 hidden_states, residual = layer(positions, hidden_states, residual)
-            hidden_states, _ = self.norm(hidden_states, residual, out=hidden_states,
-                                         residual_out=residual)
-        return hidden_states
+            return self.norm.residual_norm(residual, hidden_states)
 
 
 class Qwen2Model(DecoderModel):

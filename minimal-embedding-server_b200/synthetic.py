@@ -91,12 +91,45 @@ def pack_awq(codes: torch.Tensor) -> torch.Tensor:
 
 
 def random_awq(K: int, N: int, gen: torch.Generator, device="cpu",
-               scale_lo: float = 0.002, scale_hi: float = 0.02):
+               scale_lo: float = 0.002, scale_hi: float = 0.02, zero_lo: int = 0,
+               zero_hi: int = 15):
     q = torch.randint(0, 16, (K, N), generator=gen, device=device, dtype=torch.uint8)
-    z = torch.randint(0, 16, (K // GROUP, N), generator=gen, device=device, dtype=torch.uint8)
+    z = torch.randint(zero_lo, zero_hi + 1, (K // GROUP, N), generator=gen, device=device,
+                      dtype=torch.uint8)
     s = torch.rand((K // GROUP, N), generator=gen, device=device)
     s = (s * (scale_hi - scale_lo) + scale_lo).to(torch.float16)
     return pack_awq(q), pack_awq(z), s
+
+
+def quantize_awq(w: torch.Tensor, group: int = GROUP):
+    """Round-to-nearest asymmetric 4-bit group quantisation of a dense ``[out, in]`` weight
+    into AWQ checkpoint tensors (qweight ``[in, out/8]``, qzeros ``[in/G, out/8]``, fp16
+    scales ``[in/G, out]``): per group of ``group`` input features, s = (max - min) / 15,
+    z = clamp(round(-min / s), 0, 15), q = clamp(round(w / s) + z, 0, 15)."""
+    wt = w.t().float()                                   # [K, N]
+    K, N = wt.shape
+    g = wt.reshape(K // group, group, N)
+    lo, hi = g.amin(1), g.amax(1)
+    s = ((hi - lo).clamp(min=1e-5) / 15).to(torch.float16)
+    sf = s.float()
+    z = (-torch.round(lo / sf)).clamp(0, 15)
+    q = (torch.round(g / sf[:, None, :]) + z[:, None, :]).clamp(0, 15)
+    return (pack_awq(q.reshape(K, N).to(torch.uint8)), pack_awq(z.to(torch.uint8)), s)
+
+
+def quantize_dense_checkpoint(dense: dict) -> dict:
+    """Dense checkpoint-named weights -> AWQ checkpoint (linears quantised, embeddings and
+    biases in bf16, norms copied)."""
+    out = {}
+    for name, t in dense.items():
+        if name.endswith("_proj.weight"):
+            base = name[: -len(".weight")]
+            out[base + ".qweight"], out[base + ".qzeros"], out[base + ".scales"] = quantize_awq(t)
+        elif name.endswith(".bias") or name == "embed_tokens.weight":
+            out[name] = t.to(torch.bfloat16)
+        else:
+            out[name] = t.to(torch.bfloat16)
+    return out
 
 
 def _gen(seed: int, device) -> torch.Generator:
@@ -104,8 +137,10 @@ def _gen(seed: int, device) -> torch.Generator:
 
 
 def awq_weights(cfg, seed: int = 0, device="cpu", num_layers: int | None = None,
-                norm_noise: float = 0.0) -> dict:
-    """Checkpoint-named AWQ model tensors, generated in a fixed order from ``seed``."""
+                norm_noise: float = 0.0, zero_range: tuple[int, int] = (0, 15)) -> dict:
+    """Checkpoint-named AWQ model tensors, generated in a fixed order from ``seed``.
+    ``zero_range`` bounds the zero-point codes (the benchmark configs use [0, 15];
+    checkpoints produced by AWQ calibration sit near the midpoint, e.g. [7, 8])."""
     gen = _gen(seed, device)
     L = cfg.num_hidden_layers if num_layers is None else num_layers
     H = cfg.hidden_size
@@ -126,7 +161,8 @@ def awq_weights(cfg, seed: int = 0, device="cpu", num_layers: int | None = None,
         p = f"layers.{i}."
         out[p + "input_layernorm.weight"] = norm(H)
         for name, (K, N) in linear_shapes(cfg).items():
-            qw, qz, sc = random_awq(K, N, gen, device)
+            qw, qz, sc = random_awq(K, N, gen, device, zero_lo=zero_range[0],
+                                    zero_hi=zero_range[1])
             out[p + name + ".qweight"], out[p + name + ".qzeros"], out[p + name + ".scales"] = qw, qz, sc
             if qwen2 and name in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"):
                 out[p + name + ".bias"] = normal(N)

@@ -215,3 +215,48 @@ def test_varlen_attention(lengths, Hq, Hkv):
     assert _C.take_device_error() == 0
     err = (got - want).abs().max().item()
     assert err < 2e-2, err
+
+
+# ------------------------------------------------------------------ fp32 residual stream
+def test_embedding_f32_exact():
+    g = torch.Generator().manual_seed(16)
+    table = bf16(torch.randn(500, 1536, generator=g))
+    ids = torch.randint(0, 500, (333,), generator=g)
+    got = _C.embedding_f32(ids.to(DEV), table.to(DEV)).cpu()
+    assert got.dtype == torch.float32 and torch.equal(got, table[ids].float())
+
+
+def test_rmsnorm_f32_and_add_rmsnorm_f32res():
+    g = torch.Generator().manual_seed(17)
+    rows, H = 257, 1024
+    res = torch.randn(rows, H, generator=g) * 3
+    x = bf16(torch.randn(rows, H, generator=g))
+    w = bf16(1 + 0.1 * torch.randn(H, generator=g))
+    # Tolerance: 2 ulps, as for the bf16 variants (fp32 rsqrt moves the first rounding).
+    got = _C.rmsnorm(res.to(DEV), w.to(DEV), 1e-6).cpu()
+    assert ulp_close(got, ops.rms_norm(res, w, 1e-6).to(torch.bfloat16), 2)
+    rd = res.to(DEV)
+    y = _C.add_rmsnorm_f32res(x.to(DEV), rd, w.to(DEV), 1e-6).cpu()
+    s = x.float() + res
+    assert torch.equal(rd.cpu(), s)             # fp32 residual updated exactly
+    assert ulp_close(y, ops.rms_norm(s, w, 1e-6).to(torch.bfloat16), 2)
+
+
+@pytest.mark.parametrize("M,K,N,bias", [(5, 256, 128, False), (130, 1024, 1024, True),
+                                        (1000, 3072, 1024, False)])
+def test_awq_gemm_residual_epilogue(M, K, N, bias):
+    # R += X @ W (+ bias) in fp32: the bf16 rounding of the GEMM output is gone, so the
+    # tolerance is that of the fp32 accumulation order alone.
+    qw, qz, sc = oawq.random_awq(K, N, seed=M)
+    g = torch.Generator().manual_seed(M)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    b = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16) if bias else None
+    r0 = torch.randn(M, N, generator=g)
+    w = torch.from_numpy(oawq.bf16_bits_to_f32(oawq.dequant_bf16_bits(qw, qz, sc)))
+    ref = r0 + x.float() @ w + (b.float() if b is not None else 0)
+    rd = r0.to(DEV)
+    _C.awq_gemm_residual(x.to(DEV), _C.awq_repack(torch.from_numpy(qw).to(DEV)),
+                         torch.from_numpy(qz).to(DEV), torch.from_numpy(sc).view(torch.int16).to(DEV),
+                         rd, None if b is None else b.to(DEV))
+    err = (rd.cpu() - ref).abs().max().item()
+    assert err <= 1e-4 * ref.abs().max().item() + 1e-4, err
