@@ -139,6 +139,7 @@ int mes_varlen_cu_seqlens(const void* workspace, int64_t T, int32_t* cu_seqlens,
 int mes_varlen_attention(const void* qkv, int64_t ld, void* out, const void* workspace,
                          int64_t T, int Hq, int Hkv, int D, float scale, void* stream);
 
+
 /* ---------------------------------------------------------------------------------
  * Last-token pooling + L2 normalisation.  out[b, :] = x / max(||x||_2, 1e-12),
  * x = hidden[idx[b], :] (fp32 math and output).

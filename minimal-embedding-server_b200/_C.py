@@ -50,8 +50,9 @@ _lib = None
 # exactly one kernel); read by the benchmark to report its launch count.
 launch_count = 0
 
-# Optional per-launch timing hook for the AWQ GEMM: when set to a list, every awq_gemm
-# call appends (start_event, end_event, flops) recorded on the launching stream.
+# Optional per-launch timing hook for the AWQ GEMM: when set to a list, every awq_gemm /
+# awq_gemm_residual call appends (start_event, end_event, flops, (kind, M, N, K)) recorded
+# on the launching stream.
 gemm_events = None
 
 
@@ -294,7 +295,7 @@ def awq_gemm_residual(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.
                                        M, N, K, group_size, _stream(x)), "mes_awq_gemm_residual")
     if ev is not None:
         e1.record()
-        ev.append((e0, e1, 2.0 * M * N * K))
+        ev.append((e0, e1, 2.0 * M * N * K, ("residual", M, N, K)))
     return residual
 
 
@@ -318,5 +319,5 @@ def awq_gemm(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
                               _stream(x)), "mes_awq_gemm")
     if ev is not None:
         e1.record()
-        ev.append((e0, e1, 2.0 * M * N * K))
+        ev.append((e0, e1, 2.0 * M * N * K, ("bf16", M, N, K)))
     return out
