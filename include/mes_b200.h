@@ -139,6 +139,21 @@ int mes_varlen_cu_seqlens(const void* workspace, int64_t T, int32_t* cu_seqlens,
 int mes_varlen_attention(const void* qkv, int64_t ld, void* out, const void* workspace,
                          int64_t T, int Hq, int Hkv, int D, float scale, void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * The same schedule + attention for callers that cannot allocate device memory (an FFI
+ * caller that only holds the buffers its runtime handed over, or a serving process whose
+ * device memory is fixed in advance by its own pool).  No counterpart in the reference.
+ * The workspace is a fixed array inside this library, on every device that loads it,
+ * sized for at most mes_varlen_attention_noalloc_max_tokens() tokens (131072, ~1.5 MiB);
+ * larger T returns MES_ERR_INVALID.  Nothing is allocated.  The first call on a device
+ * looks up the array's device address (make that first call before any stream capture).
+ * Every call on a device shares the array: calls whose GPU work overlaps race.
+ * positions: i64 [T]; qkv, out, D, scale as for mes_varlen_attention.
+ * ------------------------------------------------------------------------------- */
+int64_t mes_varlen_attention_noalloc_max_tokens(void);
+int mes_varlen_attention_noalloc(const int64_t* positions, const void* qkv, int64_t ld,
+                                 void* out, int64_t T, int Hq, int Hkv, int D, float scale,
+                                 void* stream);
 
 /* ---------------------------------------------------------------------------------
  * Last-token pooling + L2 normalisation.  out[b, :] = x / max(||x||_2, 1e-12),

@@ -35,6 +35,9 @@ SIGNATURES = {
     "mes_varlen_schedule": (_i32, [_vp, _i64, _vp, _vp]),
     "mes_varlen_cu_seqlens": (_i32, [_vp, _i64, _vp, _vp, _vp]),
     "mes_varlen_attention": (_i32, [_vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp]),
+    "mes_varlen_attention_noalloc_max_tokens": (_i64, []),
+    "mes_varlen_attention_noalloc": (_i32, [_vp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _f32,
+                                            _vp]),
     "mes_last_token_l2": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _vp]),
     "mes_awq_repack": (_i32, [_vp, _i64, _i64, _vp, _vp]),
     "mes_awq_dequant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp]),

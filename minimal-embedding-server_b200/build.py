@@ -19,7 +19,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libmes_b200.so")
-SOURCES = ["capi.cu", "elementwise.cu", "awq_gemm.cu", "attention.cu"]
+SOURCES = ["capi.cu", "elementwise.cu", "awq_gemm.cu", "attention.cu", "attention_noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I", os.path.join(REPO, "include")]
