@@ -340,6 +340,8 @@ def run_mes(args):
 
 def main():
     args = parse_args()
+    import __graft_entry__
+    __graft_entry__.load_package()
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -44,7 +44,10 @@ def load_weights(model: nn.Module, weights: Iterable[tuple[str, torch.Tensor]] |
     items = weights.items() if isinstance(weights, dict) else weights
     for name, tensor in items:
         _load_one(model, name, tensor, mapping)
-    if hasattr(model, "process_weights_after_loading"):
+    # Repack for the kernels now when the model lives on a GPU (otherwise it happens on
+    # the layer's first forward, after the model is moved to its device).
+    on_gpu = any(p.is_cuda for p in model.parameters())
+    if on_gpu and hasattr(model, "process_weights_after_loading"):
         model.process_weights_after_loading()
 
 

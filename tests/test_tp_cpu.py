@@ -1,0 +1,103 @@
+"""Tensor-parallel host logic on CPU: two ``gloo`` ranks build the mes_b200 model, load one
+AWQ checkpoint through its ``weight_loader``s (column shards on the packed N axis, row
+shards on K and K/G), and run the oracle's TP forward on exactly the shards each rank
+holds, with the all-reduce after o_proj and down_proj.  The result must equal the TP=1
+forward on the full weights.  No GPU is involved (the kernels are not called)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _shards_to_dense(model, cfg):
+    """This rank's AWQ shards -> oracle-named dense fp32 weights ([out_local, in_local])."""
+    from oracle import awq as oawq
+
+    def deq(lin):
+        w = oawq.dequant_fp32(lin.qweight.numpy(), lin.qzeros.numpy(),
+                              lin.scales.view(torch.float16).numpy())
+        return torch.from_numpy(np.ascontiguousarray(w.T))  # [N_local, K_local]
+
+    m = model.model
+    W = {"embed_tokens.weight": m.embed_tokens.weight.float(), "norm.weight": m.norm.weight.float()}
+    for i, layer in enumerate(m.layers):
+        p = f"layers.{i}."
+        at, mlp = layer.self_attn, layer.mlp
+        W[p + "input_layernorm.weight"] = layer.input_layernorm.weight.float()
+        W[p + "post_attention_layernorm.weight"] = layer.post_attention_layernorm.weight.float()
+        W[p + "self_attn.q_norm.weight"] = at.q_norm.weight.float()
+        W[p + "self_attn.k_norm.weight"] = at.k_norm.weight.float()
+        qkv = deq(at.qkv_proj)
+        nq, nk = at.q_size, at.kv_size
+        for name, part in zip(("q", "k", "v"), qkv.split([nq, nk, nk])):
+            W[p + f"self_attn.{name}_proj.weight"] = part
+        if at.qkv_proj.bias is not None:
+            for name, part in zip(("q", "k", "v"), at.qkv_proj.bias.float().split([nq, nk, nk])):
+                W[p + f"self_attn.{name}_proj.bias"] = part
+        W[p + "self_attn.o_proj.weight"] = deq(at.o_proj)
+        gate, up = deq(mlp.gate_up_proj).chunk(2, 0)
+        W[p + "mlp.gate_proj.weight"], W[p + "mlp.up_proj.weight"] = gate, up
+        W[p + "mlp.down_proj.weight"] = deq(mlp.down_proj)
+    return W
+
+
+def _worker(rank, world, port, arch, result_q):
+    import sys
+    sys.path.insert(0, ROOT)
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from mes_b200 import synthetic
+    from mes_b200.models import Qwen2ForCausalLM, Qwen3ForCausalLM
+    from mes_b200.schemas.config import MESConfig
+    from mes_b200.ultils.loader import load_weights
+    from oracle import model as omodel
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.set_num_threads(2)
+    try:
+        if arch == "qwen3":
+            cfg = synthetic.qwen3_0_6b(num_hidden_layers=2, vocab_size=1000)
+            cls = Qwen3ForCausalLM
+        else:
+            cfg = synthetic.qwen2_1_5b(num_hidden_layers=2, vocab_size=1000)
+            cls = Qwen2ForCausalLM
+        ckpt = synthetic.quantize_dense_checkpoint(synthetic.dense_weights(cfg, seed=0))
+        model = cls(MESConfig(model_config=cfg))
+        load_weights(model, ckpt)                       # the product's sharding logic
+        ids, pos, last = synthetic.packed_batch([5, 40, 17], cfg.vocab_size, seed=2)
+        ids, pos, last = map(torch.from_numpy, (ids, pos, last))
+        qk = arch == "qwen3"
+        tp = omodel.embed(cfg, _shards_to_dense(model, cfg), ids, pos, last, qk_norm=qk,
+                          world=world)
+        full = omodel.embed(cfg, omodel.awq_dense_weights(ckpt), ids, pos, last, qk_norm=qk)
+        result_q.put((rank, float((tp - full).abs().max())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("arch", ["qwen3", "qwen2"])
+def test_tp2_shards_reproduce_tp1(arch):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, arch, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    results = dict(q.get(timeout=10) for _ in range(2))
+    assert max(results.values()) < 1e-5, results
