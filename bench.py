@@ -51,7 +51,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["mes", "reference"], default="mes")
-    ap.add_argument("--workload", choices=["c2", "c4", "c5"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -338,10 +338,57 @@ def run_mes(args):
     return result
 
 
+def run_gemm_micro(args):
+    """AWQ W4A16 GEMM microbenchmark on the Qwen3-Embedding-4B projection shapes (one JSON
+    line per shape and M).  Each launch is timed alone with CUDA events after a 256 MB
+    write that evicts L2; the bound is min(tensor peak, arithmetic intensity x HBM)."""
+    import torch
+    import __graft_entry__
+    __graft_entry__.build()
+    from mes_b200 import _C, synthetic
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak_burst, _, hbm, peak_kind = peaks()
+    shapes = {"qkv": (2560, 6144), "o": (4096, 2560), "gate_up": (2560, 19456), "down": (9728, 2560)}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    for name, (K, N) in shapes.items():
+        qw, qz, sc = synthetic.random_awq(K, N, gen, dev)
+        qwm, sc16 = _C.awq_repack(qw), sc.view(torch.int16)
+        for M in (16, 256, 2048, 20000, 120000):
+            x = torch.randn(M, K, generator=gen, device=dev).to(torch.bfloat16)
+            y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+            times = []
+            for it in range(args.warmup + args.steps):
+                flush.fill_(it & 0xFF)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                _C.awq_gemm(x, qwm, qz, sc16, None, y)
+                e1.record()
+                torch.cuda.synchronize()
+                if it >= args.warmup:
+                    times.append(e0.elapsed_time(e1) / 1000.0)
+            t = statistics.median(times)
+            flops = 2.0 * M * N * K
+            nbytes = K * N / 2 + (K // 128) * N * 2.5 + 2 * M * K + 2 * M * N
+            bound_tflops = min(peak_burst, flops / nbytes * hbm * 1e9 / 1e12)
+            tf = flops / t / 1e12
+            print(json.dumps({
+                "metric": "AWQ W4A16 GEMM TFLOP/s", "shape": name, "M": M, "N": N, "K": K,
+                "value": tf, "unit": "TFLOP/s", "us": t * 1e6, "steps": args.steps,
+                "frac_of_tensor_peak": tf / peak_burst, "bound": "tensor" if bound_tflops >= peak_burst else "hbm",
+                "frac_of_bound": tf / bound_tflops, "peak_kind": f"{peak_kind} bf16 burst",
+                "l2": "256 MB written between launches"}), flush=True)
+            del x, y
+
+
 def main():
     args = parse_args()
     import __graft_entry__
     __graft_entry__.load_package()
+    if args.workload == "c3" and args.impl == "mes":
+        run_gemm_micro(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -30,7 +30,6 @@ __device__ int g_err_gemm = 0;
 constexpr int kBN = 128;  // output features per tile (MMA M)
 constexpr int kBK = 64;   // k per pipeline stage (one 128-byte swizzle row of bf16)
 constexpr int kGroup = 128;
-constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA + TMEM alloc, warps 2..5 dequant/epilogue
 
 // Position of column (n % 8) inside an AWQ-packed word.
 __constant__ int kInvOrder[8] = {0, 4, 1, 5, 2, 6, 3, 7};
@@ -77,20 +76,27 @@ __device__ __forceinline__ uint32_t dq_pair(uint32_t w, const GroupParams& g) {
 }
 
 // ----------------------------------------------------------------------------------------
-template <int BT, int STAGES>
+// BT tokens per tile (the MMA's N), STAGES pipeline stages, NDQ dequant/epilogue warps
+// (4: one per TMEM lane quadrant; 8: two per quadrant, each taking half of a stage's
+// words and half of the epilogue's token chunks).
+template <int BT, int STAGES, bool kResidual, int NDQ>
 struct Cfg {
+  static constexpr int kThreads = 64 + 32 * NDQ;  // warp 0 TMA, warp 1 MMA, then NDQ warps
+  static constexpr int kHalves = NDQ / 4;
+  static constexpr int kWords = 8 / kHalves;      // packed words per dequant thread per stage
   static constexpr int kXStage = BT * kBK * 2;
   static constexpr int kWStage = (kBK / 8) * kBN * 4;
-  static constexpr int kOutBuf = 32 * 32 * 2;
+  static constexpr int kChunk = kResidual ? 16 : (BT < 32 ? BT : 32);  // tokens per epilogue step
+  static constexpr int kOutBuf = kChunk * 32 * 2;  // one staging block per epilogue warp
   static constexpr int kOffX = 0;
   static constexpr int kOffW = STAGES * kXStage;
   static constexpr int kOffOut = kOffW + STAGES * kWStage;
-  static constexpr int kOffBar = kOffOut + 4 * 2 * kOutBuf;
+  static constexpr int kOffBar = kOffOut + (kResidual ? 0 : NDQ * kOutBuf);
   static constexpr int kSmem = kOffBar + 256 + 1024;  // barriers + 1 KB alignment slack
-  static constexpr int kChunk = BT < 32 ? BT : 32;  // tokens per epilogue store
   static constexpr int kTmemNeed = BT + STAGES * 32;
   static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64
                                  : kTmemNeed <= 128 ? 128 : kTmemNeed <= 256 ? 256 : 512;
+  static_assert(NDQ == 4 || NDQ == 8, "dequant warps");
   static_assert(kTmemNeed <= 512, "TMEM budget");
   static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N");
   static_assert(kXStage % 1024 == 0, "swizzle atoms");
@@ -99,13 +105,13 @@ struct Cfg {
 // kResidual: instead of storing bf16 Y, the epilogue accumulates into a fp32 residual
 // stream, R[t, n] += acc + bias (the residual add of the decoder block fused into the
 // o_proj / down_proj GEMM).
-template <int BT, int STAGES, bool kResidual>
-__global__ void __launch_bounds__(kThreads)
+template <int BT, int STAGES, bool kResidual, int NDQ>
+__global__ void __launch_bounds__(Cfg<BT, STAGES, kResidual, NDQ>::kThreads)
 awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                 const __grid_constant__ CUtensorMap map_y, const int32_t* __restrict__ qzeros,
                 const uint16_t* __restrict__ scales, const __nv_bfloat16* __restrict__ bias,
                 float* __restrict__ R, int64_t ldr, int M, int N, int K) {
-  using C = Cfg<BT, STAGES>;
+  using C = Cfg<BT, STAGES, kResidual, NDQ>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -128,7 +134,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mes::mbar_init(&full[s], 1);
-      mes::mbar_init(&afull[s], 4);
+      mes::mbar_init(&afull[s], NDQ);
       mes::mbar_init(&empty[s], 1);
     }
     mes::mbar_init(accum, 1);
@@ -138,7 +144,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
   if (warp == 0 && lane == 0) {
     mes::tma_prefetch_desc(&map_x);
     mes::tma_prefetch_desc(&map_w);
-    mes::tma_prefetch_desc(&map_y);
+    if (!kResidual) mes::tma_prefetch_desc(&map_y);
   }
   if (warp == 1) {
     __syncwarp();
@@ -203,9 +209,10 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
       }
     }
     __syncwarp();
-  } else {
+  } else if (warp < 2 + NDQ) {
     // --------------------------- dequant + epilogue warps -----------------------------
     const int q = warp & 3;                 // TMEM lane quadrant of this warp
+    const int half = (warp - 2) / 4;        // which half of the words / token chunks
     const int row = q * 32 + lane;          // feature within the tile
     const int n = n0 + row;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
@@ -229,17 +236,18 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
       }
       if (!mes::mbar_wait_warp(&full[s], ph, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) { ok = false; break; }
       mes::tc_fence_after();
-      const uint32_t* wsrc = ws + s * (C::kWStage / 4) + row;
-      uint32_t a[32];
+      const uint32_t* wsrc = ws + s * (C::kWStage / 4) + half * C::kWords * kBN + row;
+      uint32_t a[4 * C::kWords];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < C::kWords; ++i) {
         const uint32_t w = wsrc[i * kBN];
         a[4 * i + 0] = dq_pair(w, gp);
         a[4 * i + 1] = dq_pair(w >> 4, gp);
         a[4 * i + 2] = dq_pair(w >> 8, gp);
         a[4 * i + 3] = dq_pair(w >> 12, gp);
       }
-      mes::tmem_st32(tmem_a + s * 32 + lane_off, a);
+      if constexpr (C::kWords == 8) mes::tmem_st32(tmem_a + s * 32 + lane_off, a);
+      else mes::tmem_st16(tmem_a + s * 32 + half * 16 + lane_off, a);
       mes::tmem_wait_st();
       mes::tc_fence_before();
       __syncwarp();
@@ -249,9 +257,10 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
     if (ok && mes::mbar_wait_warp(accum, 0, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
       mes::tc_fence_after();
       const float b = bias ? __bfloat162float(bias[n]) : 0.f;
-      __nv_bfloat16* mybuf = outbuf + (warp - 2) * 2 * 32 * 32;
+      __nv_bfloat16* buf = outbuf + (warp - 2) * (C::kOutBuf / 2);
+      bool stored = false;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BT; c0 += C::kChunk) {
+      for (int c0 = half * C::kChunk; c0 < BT; c0 += C::kHalves * C::kChunk) {
         uint32_t v[C::kChunk];
         if constexpr (C::kChunk == 32) mes::tmem_ld32(tmem + lane_off + c0, v);
         else mes::tmem_ld16(tmem + lane_off + c0, v);
@@ -268,9 +277,8 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
           for (int j = 0; j < C::kChunk; ++j)
             if (j < rows) rp[(int64_t)j * ldr] = rv[j] + (__uint_as_float(v[j]) + b);
         } else {
-          __nv_bfloat16* buf = mybuf + ((c0 / C::kChunk) & 1) * 32 * 32;
-          if (c0 >= 2 * C::kChunk) {
-            if (lane == 0) mes::tma_store_wait_read<1>();
+          if (stored) {  // the previous TMA store must have read the staging block
+            if (lane == 0) mes::tma_store_wait_read<0>();
             __syncwarp();
           }
 #pragma unroll
@@ -283,8 +291,327 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
             mes::tma_store_commit();
           }
           __syncwarp();
+          stored = true;
         }
       }
+      if (!kResidual) {
+        if (lane == 0) mes::tma_store_wait_all<0>();
+        __syncwarp();
+      }
+    }
+  }
+
+  mes::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    mes::tc_fence_after();
+    mes::tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// ----------------------------------------------------------------------------------------
+// Persistent variant for large M.  One CTA per SM walks the (128-feature, BT-token) tiles
+// in order (features fastest, so concurrently running CTAs share X rows in L2):
+//   warp 0      TMA: X tile, packed weight words, and the group's scales/zero words of
+//               every k-step into an SST-deep shared-memory ring;
+//   warp 1      MMA issue into one of two TMEM accumulators (tile i+1's mainloop runs
+//               while the epilogue drains tile i);
+//   warps 2..   SETS sets of four dequant warps (one per TMEM lane quadrant); set g
+//               dequantises the k-steps it with it % SETS == g, so SETS stages are in
+//               flight at once and the tcgen05.st latency of one stage overlaps the
+//               arithmetic of the next;
+//   last 4      epilogue (one per lane quadrant).
+// TMEM: accumulators at columns [0, BT) and [BT, 2BT), then an AST-deep ring of
+// dequantised A slots (32 columns each).  The shared-memory ring is deeper than the TMEM
+// ring so that TMA loads run far enough ahead of the MMA to hide their latency.
+// AST == 0 keeps the dequantised A tile in shared memory instead (one 16 KB, 128-byte
+// swizzled K-major tile per stage) and issues tcgen05.mma with both operands from shared
+// memory; TMEM then holds only the two accumulators.
+template <int BT, int SST, int AST, bool kResidual, int SETS>
+struct PCfg {
+  static constexpr int kDqWarps = 4 * SETS;
+  static constexpr int kEpiWarps = 4;
+  static constexpr int kThreads = (2 + kDqWarps + kEpiWarps) * 32;
+  static constexpr int kXStage = BT * kBK * 2;
+  static constexpr int kWBytes = (kBK / 8) * kBN * 4;  // 8 words x 128 features
+  static constexpr int kSBytes = kBN * 2;               // fp16 scales of the group
+  static constexpr int kZBytes = (kBN / 8) * 4;         // packed zero-points of the group
+  static constexpr int kWStage = kWBytes + 256 + 128;   // words | scales (256 B) | zeros (64 B)
+  static constexpr int kChunk = kResidual ? 16 : 32;
+  static constexpr int kOutBuf = kChunk * 32 * 2;
+  static constexpr int kASlots = AST == 0 ? SST : AST;
+  static constexpr int kAStage = AST == 0 ? kBN * kBK * 2 : 0;  // A tile in shared memory
+  static constexpr int kOffX = 0;
+  static constexpr int kOffA = SST * kXStage;
+  static constexpr int kOffW = kOffA + SST * kAStage;
+  static constexpr int kOffOut = kOffW + SST * kWStage;
+  static constexpr int kOffBar = kOffOut + (kResidual ? 0 : kEpiWarps * kOutBuf);
+  static constexpr int kSmem = kOffBar + 512 + 1024;
+  static constexpr int kTmemNeed = 2 * BT + AST * 32;
+  static_assert(kSmem <= 232448, "shared memory budget");
+  static_assert((2 * SST + 2 * kASlots + 4) * 8 + 8 <= 512, "barrier area");
+  static_assert(kTmemNeed <= 512, "TMEM budget");
+  static_assert(kSBytes == 256 && kZBytes == 64 && kWStage % 128 == 0, "stage layout");
+  static_assert(BT % 16 == 0 && BT <= 256 && kXStage % 1024 == 0, "tile");
+};
+
+template <int BT, int SST, int AST, bool kResidual, int SETS>
+__global__ void __launch_bounds__(PCfg<BT, SST, AST, kResidual, SETS>::kThreads, 1)
+awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
+                           const __grid_constant__ CUtensorMap map_w,
+                           const __grid_constant__ CUtensorMap map_s,
+                           const __grid_constant__ CUtensorMap map_z,
+                           const __grid_constant__ CUtensorMap map_y,
+                           const __nv_bfloat16* __restrict__ bias, float* __restrict__ R,
+                           int64_t ldr, int M, int N, int K) {
+  using C = PCfg<BT, SST, AST, kResidual, SETS>;
+  constexpr uint32_t kTmemCols = 512;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* xs = smem + C::kOffX;
+  uint8_t* as = smem + C::kOffA;
+  uint8_t* wst = smem + C::kOffW;
+  __nv_bfloat16* outbuf = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffOut);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* full = bars;                      // [SST] TMA landed
+  uint64_t* empty = bars + SST;               // [SST] MMAs of the stage done
+  uint64_t* afull = bars + 2 * SST;           // [kASlots] dequantised A written
+  uint64_t* aempty = afull + C::kASlots;      // [kASlots] MMAs reading the A slot done
+  uint64_t* acc_full = aempty + C::kASlots;   // [2] accumulator complete
+  uint64_t* acc_empty = acc_full + 2;         // [2] accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = mes::warp_id(), lane = mes::lane_id();
+  const int nk = K / kBK;
+  const int num_n = N / kBN;
+  const int num_tiles = num_n * ((M + BT - 1) / BT);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SST; ++s) {
+      mes::mbar_init(&full[s], 1);
+      mes::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < C::kASlots; ++a) {
+      mes::mbar_init(&afull[a], 4);
+      mes::mbar_init(&aempty[a], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mes::mbar_init(&acc_full[b], 1);
+      mes::mbar_init(&acc_empty[b], C::kEpiWarps);
+    }
+    *abort_flag = 0;
+    mes::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    mes::tma_prefetch_desc(&map_x);
+    mes::tma_prefetch_desc(&map_w);
+    mes::tma_prefetch_desc(&map_s);
+    mes::tma_prefetch_desc(&map_z);
+    if (!kResidual) mes::tma_prefetch_desc(&map_y);
+  }
+  if (warp == 1) {
+    __syncwarp();
+    mes::tmem_alloc(tmem_slot, kTmemCols);
+    mes::tmem_relinquish();
+  }
+  mes::tc_fence_before();
+  __syncthreads();
+  mes::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_a = tmem + 2 * BT;
+
+  if (warp == 0) {
+    // ------------------------------- TMA producer -------------------------------------
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int n0 = (tile % num_n) * kBN, t0 = (tile / num_n) * BT;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % SST;
+          if (it >= SST &&
+              !mes::mbar_wait(&empty[s], ((it / SST) & 1) ^ 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          uint8_t* w = wst + s * C::kWStage;
+          mes::mbar_arrive_expect_tx(&full[s], C::kXStage + C::kWBytes + C::kSBytes + C::kZBytes);
+          mes::tma_load_2d(xs + s * C::kXStage, &map_x, &full[s], kb * kBK, t0);
+          mes::tma_load_2d(w, &map_w, &full[s], n0, kb * (kBK / 8));
+          mes::tma_load_2d(w + C::kWBytes, &map_s, &full[s], n0, kb / 2);
+          mes::tma_load_2d(w + C::kWBytes + 256, &map_z, &full[s], n0 / 8, kb / 2);
+        }
+      }
+      if (!ok) {
+        const uint64_t t = mes::globaltimer_ns();  // let issued copies land
+        while (mes::globaltimer_ns() - t < 1000000ull) {
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------- MMA issuer ---------------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = mes::idesc_bf16_f32(kBN, BT, false);
+      const uint32_t xs_addr = mes::smem_u32(xs), as_addr = mes::smem_u32(as);
+      int it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++lt) {
+        const int b = lt & 1;
+        if (lt >= 2 &&
+            !mes::mbar_wait(&acc_empty[b], ((lt >> 1) - 1) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
+          ok = false;
+          break;
+        }
+        mes::tc_fence_after();
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % SST, a = it % C::kASlots;
+          if (!mes::mbar_wait(&full[s], (it / SST) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT) ||
+              !mes::mbar_wait(&afull[a], (it / C::kASlots) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          mes::tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t bdesc = mes::smem_desc_sw128(xs_addr + s * C::kXStage + kk * 32, 16, 1024);
+            if constexpr (AST == 0) {
+              const uint64_t adesc = mes::smem_desc_sw128(as_addr + s * C::kAStage + kk * 32, 16, 1024);
+              mes::mma_ss(tmem + b * BT, adesc, bdesc, idesc, (kb | kk) != 0);
+            } else {
+              mes::mma_ts(tmem + b * BT, tmem_a + a * 32 + kk * 8, bdesc, idesc, (kb | kk) != 0);
+            }
+          }
+          mes::tc_commit(&empty[s]);
+          if constexpr (AST != 0) mes::tc_commit(&aempty[a]);
+        }
+        mes::tc_commit(&acc_full[b]);
+      }
+      if (!ok) {
+        const uint64_t t = mes::globaltimer_ns();  // let issued MMAs finish
+        while (mes::globaltimer_ns() - t < 1000000ull) {
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp < 2 + C::kDqWarps) {
+    // --------------------------------- dequant ----------------------------------------
+    const int q = warp & 3;
+    const int set = (warp - 2) / 4;
+    const int row = q * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const int zshift = 4 * kInvOrder[row & 7];  // n0 is a multiple of 128
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        if (it % SETS != set) continue;
+        const int s = it % SST, a = it % C::kASlots;
+        // With A in shared memory the stage's own ring protects it (the producer refills
+        // a stage only after its MMAs completed); with A in TMEM its slot is waited for.
+        if (!mes::mbar_wait_warp(&full[s], (it / SST) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT) ||
+            (AST != 0 && it >= AST &&
+             !mes::mbar_wait_warp(&aempty[a], ((it / C::kASlots) & 1) ^ 1, abort_flag,
+                                  &g_err_gemm, MES_ERR_TIMEOUT))) {
+          ok = false;
+          break;
+        }
+        mes::tc_fence_after();
+        const uint8_t* w = wst + s * C::kWStage;
+        const GroupParams gp =
+            make_group(reinterpret_cast<const uint32_t*>(w + C::kWBytes + 256)[row >> 3], zshift,
+                       reinterpret_cast<const uint16_t*>(w + C::kWBytes)[row]);
+        const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(w) + row;
+        uint32_t av[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t v = wsrc[i * kBN];
+          av[4 * i + 0] = dq_pair(v, gp);
+          av[4 * i + 1] = dq_pair(v >> 4, gp);
+          av[4 * i + 2] = dq_pair(v >> 8, gp);
+          av[4 * i + 3] = dq_pair(v >> 12, gp);
+        }
+        if constexpr (AST == 0) {
+          // Row `row` of the 128 x 64 K-major tile, 128-byte swizzle: 16-byte chunk i
+          // (k = 8i .. 8i+7) lives at chunk position i ^ (row & 7).
+          uint8_t* arow = as + s * C::kAStage + row * 128;
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<uint4*>(arow + ((i ^ (row & 7)) * 16)) =
+                make_uint4(av[4 * i], av[4 * i + 1], av[4 * i + 2], av[4 * i + 3]);
+          mes::fence_proxy_async_smem();
+        } else {
+          mes::tmem_st32(tmem_a + a * 32 + lane_off, av);
+          mes::tmem_wait_st();
+        }
+        mes::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mes::mbar_arrive(&afull[a]);
+        __syncwarp();
+      }
+    }
+  } else {
+    // --------------------------------- epilogue ---------------------------------------
+    const int q = warp & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    __nv_bfloat16* buf = outbuf + (warp - 2 - C::kDqWarps) * (C::kOutBuf / 2);
+    bool stored = false;
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
+      const int b = lt & 1;
+      const int n0 = (tile % num_n) * kBN, t0 = (tile / num_n) * BT;
+      const int n = n0 + q * 32 + lane;
+      if (!mes::mbar_wait_warp(&acc_full[b], (lt >> 1) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT))
+        break;
+      mes::tc_fence_after();
+      const float bv = bias ? __bfloat162float(bias[n]) : 0.f;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BT; c0 += C::kChunk) {
+        uint32_t v[C::kChunk];
+        if constexpr (C::kChunk == 32) mes::tmem_ld32(tmem + lane_off + b * BT + c0, v);
+        else mes::tmem_ld16(tmem + lane_off + b * BT + c0, v);
+        mes::tmem_wait_ld();
+        if (t0 + c0 >= M) continue;  // rows past the end of X
+        if constexpr (kResidual) {
+          const int rows = min(C::kChunk, M - (t0 + c0));
+          float* rp = R + (int64_t)(t0 + c0) * ldr + n;
+          float rv[C::kChunk];
+#pragma unroll
+          for (int j = 0; j < C::kChunk; ++j) rv[j] = j < rows ? rp[(int64_t)j * ldr] : 0.f;
+#pragma unroll
+          for (int j = 0; j < C::kChunk; ++j)
+            if (j < rows) rp[(int64_t)j * ldr] = rv[j] + (__uint_as_float(v[j]) + bv);
+        } else {
+          if (stored) {
+            if (lane == 0) mes::tma_store_wait_read<0>();
+            __syncwarp();
+          }
+#pragma unroll
+          for (int j = 0; j < C::kChunk; j += 2) {  // one bf16x2 conversion per two values
+            const uint32_t pk = mes::pack_bf16x2(__uint_as_float(v[j]) + bv, __uint_as_float(v[j + 1]) + bv);
+            buf[j * 32 + lane] = __ushort_as_bfloat16(static_cast<unsigned short>(pk & 0xFFFFu));
+            buf[(j + 1) * 32 + lane] = __ushort_as_bfloat16(static_cast<unsigned short>(pk >> 16));
+          }
+          mes::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mes::tma_store_2d(&map_y, buf, n0 + q * 32, t0 + c0);
+            mes::tma_store_commit();
+          }
+          __syncwarp();
+          stored = true;
+        }
+      }
+      // The accumulator is free once every tcgen05.ld above has completed.
+      mes::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mes::mbar_arrive(&acc_empty[b]);
+      __syncwarp();
+    }
+    if (!kResidual) {
       if (lane == 0) mes::tma_store_wait_all<0>();
       __syncwarp();
     }
@@ -295,7 +622,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
   if (warp == 1) {
     __syncwarp();
     mes::tc_fence_after();
-    mes::tmem_dealloc(tmem, C::kTmemCols);
+    mes::tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -341,12 +668,12 @@ __global__ void awq_dequant_kernel(const uint32_t* __restrict__ qw, const int32_
   }
 }
 
-template <int BT, int STAGES, bool kResidual>
+template <int BT, int STAGES, bool kResidual, int NDQ>
 int launch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
                 const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
                 int64_t N, int64_t K, cudaStream_t stream) {
-  using C = Cfg<BT, STAGES>;
-  cudaError_t e = cudaFuncSetAttribute(awq_gemm_kernel<BT, STAGES, kResidual>,
+  using C = Cfg<BT, STAGES, kResidual, NDQ>;
+  cudaError_t e = cudaFuncSetAttribute(awq_gemm_kernel<BT, STAGES, kResidual, NDQ>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   if (e != cudaSuccess) return MES_ERR_CUDA;
   CUtensorMap mx, mw, my;
@@ -362,20 +689,77 @@ int launch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qz
     return MES_ERR_INVALID;
   }
   dim3 grid((unsigned)(N / kBN), (unsigned)((M + BT - 1) / BT));
-  awq_gemm_kernel<BT, STAGES, kResidual><<<grid, kThreads, C::kSmem, stream>>>(
+  awq_gemm_kernel<BT, STAGES, kResidual, NDQ><<<grid, C::kThreads, C::kSmem, stream>>>(
       mx, mw, my, qzeros, (const uint16_t*)scales, (const __nv_bfloat16*)bias,
       kResidual ? (float*)Y : nullptr, ldy, (int)M, (int)N, (int)K);
   return mes_host::from_cuda(cudaGetLastError());
+}
+
+template <int BT, int SST, int AST, bool kResidual, int SETS>
+int launch_gemm_persistent(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
+                           const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
+                           int64_t N, int64_t K, cudaStream_t stream) {
+  using C = PCfg<BT, SST, AST, kResidual, SETS>;
+  cudaError_t e = cudaFuncSetAttribute(awq_gemm_persistent_kernel<BT, SST, AST, kResidual, SETS>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  if (e != cudaSuccess) return MES_ERR_CUDA;
+  CUtensorMap mx, mw, ms, mz, my;
+  if (!mes_host::make_map_2d(&mx, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, ldx, BT, kBK,
+                             CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !mes_host::make_map_2d(&mw, qw, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, K / 8, N, N, kBK / 8, kBN,
+                             CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !mes_host::make_map_2d(&ms, scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, K / kGroup, N, N, 1,
+                             kBN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !mes_host::make_map_2d(&mz, qzeros, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, K / kGroup, N / 8,
+                             N / 8, 1, kBN / 8, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return MES_ERR_INVALID;
+  if (kResidual) {
+    my = mx;  // unused by the residual epilogue
+  } else if (!mes_host::make_map_2d(&my, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, N, ldy,
+                                    C::kChunk, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+    return MES_ERR_INVALID;
+  }
+  const int64_t tiles = (N / kBN) * ((M + BT - 1) / BT);
+  const int grid = (int)(tiles < mes_host::sm_count() ? tiles : mes_host::sm_count());
+  awq_gemm_persistent_kernel<BT, SST, AST, kResidual, SETS><<<grid, C::kThreads, C::kSmem, stream>>>(
+      mx, mw, ms, mz, my, (const __nv_bfloat16*)bias, kResidual ? (float*)Y : nullptr, ldy,
+      (int)M, (int)N, (int)K);
+  return mes_host::from_cuda(cudaGetLastError());
+}
+
+// Tile configuration for M > 64 tokens.  The environment variable MES_GEMM_CONFIG (read
+// once) selects among the compiled variants for tuning: 0 = 128 tokens / 4 dequant warps,
+// 1 = 128 tokens / 8 dequant warps, 2 = 256 tokens / 8 dequant warps; persistent with
+// double-buffered accumulators: 3 = 192 tokens, 4 smem / 4 TMEM stages; 4 = 192 tokens,
+// 7 / 4 stages; 5 = 128 tokens, 8 / 8 stages; A tile in shared memory: 6 = 256 tokens,
+// 4 stages (default: reading A from TMEM measured ~1.3x slower per MMA than from shared
+// memory for this shape); 7 = 192 tokens, 4 stages.
+int large_m_config() {
+  static int cfg = [] {
+    const char* v = getenv("MES_GEMM_CONFIG");
+    int c = v ? atoi(v) : 6;
+    return (c < 0 || c > 7) ? 6 : c;
+  }();
+  return cfg;
 }
 
 template <bool kResidual>
 int dispatch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
                   const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
                   int64_t N, int64_t K, cudaStream_t s) {
-  if (M <= 16) return launch_gemm<16, 6, kResidual>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-  if (M <= 32) return launch_gemm<32, 6, kResidual>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-  if (M <= 64) return launch_gemm<64, 6, kResidual>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-  return launch_gemm<128, 4, kResidual>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  if (M <= 16) return launch_gemm<16, 6, kResidual, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  if (M <= 32) return launch_gemm<32, 6, kResidual, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  if (M <= 64) return launch_gemm<64, 6, kResidual, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  switch (large_m_config()) {
+    case 0: return launch_gemm<128, 4, kResidual, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+    case 2: return launch_gemm<256, 4, kResidual, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+    case 3: return launch_gemm_persistent<192, 4, 4, kResidual, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+    case 4: return launch_gemm_persistent<192, 7, 4, kResidual, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+    case 5: return launch_gemm_persistent<128, 8, 8, kResidual, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+    case 6: return launch_gemm_persistent<256, 4, 0, kResidual, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+    case 7: return launch_gemm_persistent<192, 4, 0, kResidual, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+    default: return launch_gemm<128, 4, kResidual, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  }
 }
 
 int check_gemm_args(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,

@@ -71,8 +71,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort_flag, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (true) {
+  for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (n & 63) continue;  // the abort flag and the clock are checked every 64 polls
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       *abort_flag = 1;

@@ -260,3 +260,44 @@ def test_awq_gemm_residual_epilogue(M, K, N, bias):
                          rd, None if b is None else b.to(DEV))
     err = (rd.cpu() - ref).abs().max().item()
     assert err <= 1e-4 * ref.abs().max().item() + 1e-4, err
+
+
+# ------------------------------------------------------------------ GEMM tile variants
+_VARIANT_CHECK = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+import __graft_entry__; __graft_entry__.load_package()
+from mes_b200 import _C
+from oracle import awq as oawq
+for M, K, N, res in [(65, 256, 128, False), (300, 1024, 384, True), (777, 3072, 1024, False), (1000, 1024, 256, True)]:
+    qw, qz, sc = oawq.random_awq(K, N, seed=M)
+    g = torch.Generator().manual_seed(M)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = torch.from_numpy(oawq.bf16_bits_to_f32(oawq.dequant_bf16_bits(qw, qz, sc)))
+    ref = x.float() @ w
+    args = (x.cuda(), _C.awq_repack(torch.from_numpy(qw).cuda()), torch.from_numpy(qz).cuda(),
+            torch.from_numpy(sc).view(torch.int16).cuda())
+    if res:
+        r = torch.zeros(M, N, device="cuda")
+        got = _C.awq_gemm_residual(*args, r).cpu()
+        tol = 1e-4 * ref.abs().max().item() + 1e-4
+    else:
+        got = _C.awq_gemm(*args).float().cpu()
+        tol = 1e-2 * ref.abs().max().item() + 1e-3
+    err = (got - ref).abs().max().item()
+    assert err <= tol, (M, K, N, res, err, tol)
+assert _C.take_device_error() == 0
+print("ok")
+"""
+
+
+@pytest.mark.parametrize("config", ["0", "1", "2", "3", "4", "5", "6", "7"])
+def test_awq_gemm_tile_variants(config):
+    # The large-M tile variant is chosen once per process (MES_GEMM_CONFIG), so each runs
+    # in a child process; same tolerances as test_awq_gemm_matches_fp32 and the residual test.
+    import os, subprocess, sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, MES_GEMM_CONFIG=config)
+    r = subprocess.run([sys.executable, "-c", _VARIANT_CHECK, root], env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-3000:]
