@@ -195,6 +195,17 @@ int mes_awq_gemm(const void* X, int64_t ldx, const int32_t* qweight_mes,
                  const int32_t* qzeros, const void* scales, const void* bias, void* Y,
                  int64_t ldy, int64_t M, int64_t N, int64_t K, int group_size, void* stream);
 
+/* Gate/up projection fused with SiLU-and-mul: Y[M, N/2] = bf16(silu(X Wg) * (X Wu)), fp32
+ * math on the accumulators.  Replaces MergedColumnParallelLinear.forward followed by
+ * SiluAndMul.forward (layers/linear.py:90-107, layers/activation.py:12-14, composed at
+ * models/qwen2.py:113-117).  The weight's N = 2I columns must be interleaved in blocks of
+ * 16: columns [32b, 32b+16) hold gate features 16b.., columns [32b+16, 32b+32) the up
+ * features 16b..; output column 16b + j = silu(gate_{16b+j}) * up_{16b+j}.  qzeros /
+ * scales are permuted the same way.  N % 128 == 0, ldy >= N/2. */
+int mes_awq_gemm_silu(const void* X, int64_t ldx, const int32_t* qweight_mes,
+                      const int32_t* qzeros, const void* scales, void* Y, int64_t ldy, int64_t M,
+                      int64_t N, int64_t K, int group_size, void* stream);
+
 /* Same product accumulated into a f32 residual stream: R[M, N] += X * W (+ bias), pitch ldr
  * elements.  This is RowParallelLinear.forward (layers/linear.py:176-180) at tp == 1 fused
  * with the residual add of the following RMSNorm.add_rms_forward (layers/layernorm.py:36),

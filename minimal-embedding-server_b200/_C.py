@@ -45,6 +45,7 @@ SIGNATURES = {
                             _vp]),
     "mes_awq_gemm_residual": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                      _i32, _vp]),
+    "mes_awq_gemm_silu": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp]),
 }
 
 _lib = None
@@ -300,6 +301,45 @@ def awq_gemm_residual(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.
         e1.record()
         ev.append((e0, e1, 2.0 * M * N * K, ("residual", M, N, K)))
     return residual
+
+
+def awq_gemm_silu(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
+                  scales: torch.Tensor, out: torch.Tensor | None = None,
+                  group_size: int = 128) -> torch.Tensor:
+    """``silu(x @ Wg) * (x @ Wu)`` with the gate/up columns interleaved in blocks of 16
+    (see ``interleave_gate_up``); output ``[M, N/2]`` bf16."""
+    _need(x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(-1) == 1,
+          "x must be bf16 [M, K] with unit inner stride")
+    K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
+    M = x.shape[0]
+    _need(x.shape[1] == K, f"x has K={x.shape[1]}, weight has K={K}")
+    if out is None:
+        out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=x.device)
+    ev = gemm_events
+    if ev is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+    _check(lib().mes_awq_gemm_silu(_p(x), x.stride(0), _p(qweight_mes), _p(qzeros), _p(scales),
+                                   _p(out), out.stride(0), M, N, K, group_size, _stream(x)),
+           "mes_awq_gemm_silu")
+    if ev is not None:
+        e1.record()
+        ev.append((e0, e1, 2.0 * M * N * K, ("silu", M, N, K)))
+    return out
+
+
+def interleave_gate_up(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor):
+    """Permute AWQ tensors of a ``[gate | up]`` projection (N = 2I columns) so that blocks of
+    16 gate and 16 up columns alternate, the layout ``mes_awq_gemm_silu`` expects."""
+    N = scales.shape[1]
+    I = N // 2
+    _need(I % 16 == 0, "the intermediate size per rank must be a multiple of 16")
+    blocks = torch.arange(I // 16, device=scales.device)
+    cols = torch.stack([blocks * 16, I + blocks * 16], dim=1).reshape(-1)        # block starts
+    perm = (cols[:, None] + torch.arange(16, device=scales.device)).reshape(-1)  # [N]
+    perm8 = perm[::8] // 8                                                       # packed columns
+    return (qweight.index_select(1, perm8).contiguous(), qzeros.index_select(1, perm8).contiguous(),
+            scales.index_select(1, perm).contiguous())
 
 
 def awq_gemm(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,

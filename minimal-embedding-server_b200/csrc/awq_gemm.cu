@@ -27,6 +27,51 @@ namespace {
 
 __device__ int g_err_gemm = 0;
 
+// Epilogue modes of the GEMM kernels.
+//   kEpiBf16:     Y = bf16(acc + bias)
+//   kEpiResidual: R (fp32) += acc + bias      (o_proj / down_proj into the residual stream)
+//   kEpiSilu:     Y = bf16(silu(gate) * up)   (gate_up with SiLU-and-mul; the weight columns
+//                 are interleaved in blocks of 16 - columns [32b, 32b+16) hold gate features
+//                 16b.., [32b+16, 32b+32) the matching up features - so every TMEM lane
+//                 quadrant holds both halves of its 16 outputs; Y has N/2 columns)
+constexpr int kEpiBf16 = 0, kEpiResidual = 1, kEpiSilu = 2;
+
+
+// SiLU-and-mul epilogue of one chunk of CHUNK tokens for one warp.  Lane l < 16 holds the
+// gate feature and lane l + 16 the matching up feature of output column `x + l`; one
+// shuffle per token pair gives lane l the up values of the first half of the chunk and
+// lane l + 16 the gate values of the second half, so each lane produces CHUNK / 2 outputs.
+template <int CHUNK>
+__device__ __forceinline__ void silu_chunk(const uint32_t (&v)[CHUNK], int lane,
+                                           __nv_bfloat16* buf, bool& stored,
+                                           const CUtensorMap* map_y, int x, int y) {
+  constexpr int H = CHUNK / 2;
+  const bool lo = lane < 16;
+  const int f = lane & 15;
+  if (stored) {
+    if (lane == 0) mes::tma_store_wait_read<0>();
+    __syncwarp();
+  }
+#pragma unroll
+  for (int j = 0; j < H; ++j) {
+    // lo lanes send their gate value of token H + j and receive the up value of token j.
+    const float send = __uint_as_float(lo ? v[H + j] : v[j]);
+    const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+    const float g = lo ? __uint_as_float(v[j]) : recv;
+    const float u = lo ? recv : __uint_as_float(v[H + j]);
+    const float o = g * __frcp_rn(1.0f + __expf(-g)) * u;
+    buf[((lo ? 0 : H) + j) * 16 + f] = __float2bfloat16_rn(o);
+  }
+  mes::fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    mes::tma_store_2d(map_y, buf, x, y);
+    mes::tma_store_commit();
+  }
+  __syncwarp();
+  stored = true;
+}
+
 constexpr int kBN = 128;  // output features per tile (MMA M)
 constexpr int kBK = 64;   // k per pipeline stage (one 128-byte swizzle row of bf16)
 constexpr int kGroup = 128;
@@ -79,8 +124,9 @@ __device__ __forceinline__ uint32_t dq_pair(uint32_t w, const GroupParams& g) {
 // BT tokens per tile (the MMA's N), STAGES pipeline stages, NDQ dequant/epilogue warps
 // (4: one per TMEM lane quadrant; 8: two per quadrant, each taking half of a stage's
 // words and half of the epilogue's token chunks).
-template <int BT, int STAGES, bool kResidual, int NDQ>
+template <int BT, int STAGES, int EPI, int NDQ>
 struct Cfg {
+  static constexpr bool kResidual = EPI == kEpiResidual, kSilu = EPI == kEpiSilu;
   static constexpr int kThreads = 64 + 32 * NDQ;  // warp 0 TMA, warp 1 MMA, then NDQ warps
   static constexpr int kHalves = NDQ / 4;
   static constexpr int kWords = 8 / kHalves;      // packed words per dequant thread per stage
@@ -102,16 +148,14 @@ struct Cfg {
   static_assert(kXStage % 1024 == 0, "swizzle atoms");
 };
 
-// kResidual: instead of storing bf16 Y, the epilogue accumulates into a fp32 residual
-// stream, R[t, n] += acc + bias (the residual add of the decoder block fused into the
-// o_proj / down_proj GEMM).
-template <int BT, int STAGES, bool kResidual, int NDQ>
-__global__ void __launch_bounds__(Cfg<BT, STAGES, kResidual, NDQ>::kThreads)
+// EPI selects the epilogue (kEpiBf16 / kEpiResidual / kEpiSilu, see their definition).
+template <int BT, int STAGES, int EPI, int NDQ>
+__global__ void __launch_bounds__(Cfg<BT, STAGES, EPI, NDQ>::kThreads)
 awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                 const __grid_constant__ CUtensorMap map_y, const int32_t* __restrict__ qzeros,
                 const uint16_t* __restrict__ scales, const __nv_bfloat16* __restrict__ bias,
                 float* __restrict__ R, int64_t ldr, int M, int N, int K) {
-  using C = Cfg<BT, STAGES, kResidual, NDQ>;
+  using C = Cfg<BT, STAGES, EPI, NDQ>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -125,6 +169,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
   uint64_t* accum = bars + 3 * STAGES;    // all MMAs done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
 
   const int warp = mes::warp_id(), lane = mes::lane_id();
   const int n0 = blockIdx.x * kBN;
@@ -144,7 +189,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
   if (warp == 0 && lane == 0) {
     mes::tma_prefetch_desc(&map_x);
     mes::tma_prefetch_desc(&map_w);
-    if (!kResidual) mes::tma_prefetch_desc(&map_y);
+    if (!C::kResidual) mes::tma_prefetch_desc(&map_y);
   }
   if (warp == 1) {
     __syncwarp();
@@ -266,7 +311,9 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
         else mes::tmem_ld16(tmem + lane_off + c0, v);
         mes::tmem_wait_ld();
         if (t0 + c0 >= M) break;  // rows past the end of X: nothing to store
-        if constexpr (kResidual) {
+        if constexpr (C::kSilu) {
+          silu_chunk<C::kChunk>(v, lane, buf, stored, &map_y, n0 / 2 + q * 16, t0 + c0);
+        } else if constexpr (C::kResidual) {
           // Each lane owns feature n; a warp touches 32 consecutive fp32 per token row.
           const int rows = min(C::kChunk, M - (t0 + c0));
           float* rp = R + (int64_t)(t0 + c0) * ldr + n;
@@ -294,7 +341,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
           stored = true;
         }
       }
-      if (!kResidual) {
+      if (!C::kResidual) {
         if (lane == 0) mes::tma_store_wait_all<0>();
         __syncwarp();
       }
@@ -321,17 +368,18 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
 //               dequantises the k-steps it with it % SETS == g, so SETS stages are in
 //               flight at once and the tcgen05.st latency of one stage overlaps the
 //               arithmetic of the next;
-//   last 4      epilogue (one per lane quadrant).
+//   last 8      epilogue (two per lane quadrant, alternating token chunks).
 // TMEM: accumulators at columns [0, BT) and [BT, 2BT), then an AST-deep ring of
 // dequantised A slots (32 columns each).  The shared-memory ring is deeper than the TMEM
 // ring so that TMA loads run far enough ahead of the MMA to hide their latency.
 // AST == 0 keeps the dequantised A tile in shared memory instead (one 16 KB, 128-byte
 // swizzled K-major tile per stage) and issues tcgen05.mma with both operands from shared
 // memory; TMEM then holds only the two accumulators.
-template <int BT, int SST, int AST, bool kResidual, int SETS>
+template <int BT, int SST, int AST, int EPI, int SETS>
 struct PCfg {
+  static constexpr bool kResidual = EPI == kEpiResidual, kSilu = EPI == kEpiSilu;
   static constexpr int kDqWarps = 4 * SETS;
-  static constexpr int kEpiWarps = 4;
+  static constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, alternating chunks
   static constexpr int kThreads = (2 + kDqWarps + kEpiWarps) * 32;
   static constexpr int kXStage = BT * kBK * 2;
   static constexpr int kWBytes = (kBK / 8) * kBN * 4;  // 8 words x 128 features
@@ -356,8 +404,8 @@ struct PCfg {
   static_assert(BT % 16 == 0 && BT <= 256 && kXStage % 1024 == 0, "tile");
 };
 
-template <int BT, int SST, int AST, bool kResidual, int SETS>
-__global__ void __launch_bounds__(PCfg<BT, SST, AST, kResidual, SETS>::kThreads, 1)
+template <int BT, int SST, int AST, int EPI, int SETS>
+__global__ void __launch_bounds__(PCfg<BT, SST, AST, EPI, SETS>::kThreads, 1)
 awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
                            const __grid_constant__ CUtensorMap map_w,
                            const __grid_constant__ CUtensorMap map_s,
@@ -365,7 +413,7 @@ awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
                            const __grid_constant__ CUtensorMap map_y,
                            const __nv_bfloat16* __restrict__ bias, float* __restrict__ R,
                            int64_t ldr, int M, int N, int K) {
-  using C = PCfg<BT, SST, AST, kResidual, SETS>;
+  using C = PCfg<BT, SST, AST, EPI, SETS>;
   constexpr uint32_t kTmemCols = 512;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -383,6 +431,7 @@ awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
   uint64_t* acc_empty = acc_full + 2;         // [2] accumulator drained
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
 
   const int warp = mes::warp_id(), lane = mes::lane_id();
   const int nk = K / kBK;
@@ -410,7 +459,7 @@ awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
     mes::tma_prefetch_desc(&map_w);
     mes::tma_prefetch_desc(&map_s);
     mes::tma_prefetch_desc(&map_z);
-    if (!kResidual) mes::tma_prefetch_desc(&map_y);
+    if (!C::kResidual) mes::tma_prefetch_desc(&map_y);
   }
   if (warp == 1) {
     __syncwarp();
@@ -556,6 +605,7 @@ awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
   } else {
     // --------------------------------- epilogue ---------------------------------------
     const int q = warp & 3;
+    const int eh = (warp - 2 - C::kDqWarps) / 4;  // which alternate chunks this warp drains
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     __nv_bfloat16* buf = outbuf + (warp - 2 - C::kDqWarps) * (C::kOutBuf / 2);
     bool stored = false;
@@ -569,13 +619,15 @@ awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
       mes::tc_fence_after();
       const float bv = bias ? __bfloat162float(bias[n]) : 0.f;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BT; c0 += C::kChunk) {
+      for (int c0 = eh * C::kChunk; c0 < BT; c0 += 2 * C::kChunk) {
         uint32_t v[C::kChunk];
         if constexpr (C::kChunk == 32) mes::tmem_ld32(tmem + lane_off + b * BT + c0, v);
         else mes::tmem_ld16(tmem + lane_off + b * BT + c0, v);
         mes::tmem_wait_ld();
         if (t0 + c0 >= M) continue;  // rows past the end of X
-        if constexpr (kResidual) {
+        if constexpr (C::kSilu) {
+          silu_chunk<C::kChunk>(v, lane, buf, stored, &map_y, n0 / 2 + q * 16, t0 + c0);
+        } else if constexpr (C::kResidual) {
           const int rows = min(C::kChunk, M - (t0 + c0));
           float* rp = R + (int64_t)(t0 + c0) * ldr + n;
           float rv[C::kChunk];
@@ -611,7 +663,7 @@ awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
       if (lane == 0) mes::mbar_arrive(&acc_empty[b]);
       __syncwarp();
     }
-    if (!kResidual) {
+    if (!C::kResidual) {
       if (lane == 0) mes::tma_store_wait_all<0>();
       __syncwarp();
     }
@@ -668,12 +720,24 @@ __global__ void awq_dequant_kernel(const uint32_t* __restrict__ qw, const int32_
   }
 }
 
-template <int BT, int STAGES, bool kResidual, int NDQ>
+// Output tensor map of an epilogue mode: bf16 Y [M, N], or Y [M, N/2] for SiLU-and-mul.
+inline bool make_out_map(CUtensorMap* my, const CUtensorMap& fallback, int epi, void* Y, int64_t M,
+                         int64_t N, int64_t ldy, int chunk) {
+  if (epi == kEpiResidual) {
+    *my = fallback;  // unused by the residual epilogue
+    return true;
+  }
+  const int64_t cols = epi == kEpiSilu ? N / 2 : N;
+  return mes_host::make_map_2d(my, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, cols, ldy, chunk,
+                               epi == kEpiSilu ? 16 : 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+template <int BT, int STAGES, int EPI, int NDQ>
 int launch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
                 const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
                 int64_t N, int64_t K, cudaStream_t stream) {
-  using C = Cfg<BT, STAGES, kResidual, NDQ>;
-  cudaError_t e = cudaFuncSetAttribute(awq_gemm_kernel<BT, STAGES, kResidual, NDQ>,
+  using C = Cfg<BT, STAGES, EPI, NDQ>;
+  cudaError_t e = cudaFuncSetAttribute(awq_gemm_kernel<BT, STAGES, EPI, NDQ>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   if (e != cudaSuccess) return MES_ERR_CUDA;
   CUtensorMap mx, mw, my;
@@ -682,25 +746,20 @@ int launch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qz
       !mes_host::make_map_2d(&mw, qw, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, K / 8, N, N, kBK / 8, kBN,
                              CU_TENSOR_MAP_SWIZZLE_NONE))
     return MES_ERR_INVALID;
-  if (kResidual) {
-    my = mx;  // unused by the residual epilogue
-  } else if (!mes_host::make_map_2d(&my, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, N, ldy,
-                                    C::kChunk, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) {
-    return MES_ERR_INVALID;
-  }
+  if (!make_out_map(&my, mx, EPI, Y, M, N, ldy, C::kChunk)) return MES_ERR_INVALID;
   dim3 grid((unsigned)(N / kBN), (unsigned)((M + BT - 1) / BT));
-  awq_gemm_kernel<BT, STAGES, kResidual, NDQ><<<grid, C::kThreads, C::kSmem, stream>>>(
+  awq_gemm_kernel<BT, STAGES, EPI, NDQ><<<grid, C::kThreads, C::kSmem, stream>>>(
       mx, mw, my, qzeros, (const uint16_t*)scales, (const __nv_bfloat16*)bias,
-      kResidual ? (float*)Y : nullptr, ldy, (int)M, (int)N, (int)K);
+      C::kResidual ? (float*)Y : nullptr, ldy, (int)M, (int)N, (int)K);
   return mes_host::from_cuda(cudaGetLastError());
 }
 
-template <int BT, int SST, int AST, bool kResidual, int SETS>
+template <int BT, int SST, int AST, int EPI, int SETS>
 int launch_gemm_persistent(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
                            const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
                            int64_t N, int64_t K, cudaStream_t stream) {
-  using C = PCfg<BT, SST, AST, kResidual, SETS>;
-  cudaError_t e = cudaFuncSetAttribute(awq_gemm_persistent_kernel<BT, SST, AST, kResidual, SETS>,
+  using C = PCfg<BT, SST, AST, EPI, SETS>;
+  cudaError_t e = cudaFuncSetAttribute(awq_gemm_persistent_kernel<BT, SST, AST, EPI, SETS>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   if (e != cudaSuccess) return MES_ERR_CUDA;
   CUtensorMap mx, mw, ms, mz, my;
@@ -713,62 +772,50 @@ int launch_gemm_persistent(const void* X, int64_t ldx, const int32_t* qw, const 
       !mes_host::make_map_2d(&mz, qzeros, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, K / kGroup, N / 8,
                              N / 8, 1, kBN / 8, CU_TENSOR_MAP_SWIZZLE_NONE))
     return MES_ERR_INVALID;
-  if (kResidual) {
-    my = mx;  // unused by the residual epilogue
-  } else if (!mes_host::make_map_2d(&my, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, N, ldy,
-                                    C::kChunk, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) {
-    return MES_ERR_INVALID;
-  }
+  if (!make_out_map(&my, mx, EPI, Y, M, N, ldy, C::kChunk)) return MES_ERR_INVALID;
   const int64_t tiles = (N / kBN) * ((M + BT - 1) / BT);
   const int grid = (int)(tiles < mes_host::sm_count() ? tiles : mes_host::sm_count());
-  awq_gemm_persistent_kernel<BT, SST, AST, kResidual, SETS><<<grid, C::kThreads, C::kSmem, stream>>>(
-      mx, mw, ms, mz, my, (const __nv_bfloat16*)bias, kResidual ? (float*)Y : nullptr, ldy,
+  awq_gemm_persistent_kernel<BT, SST, AST, EPI, SETS><<<grid, C::kThreads, C::kSmem, stream>>>(
+      mx, mw, ms, mz, my, (const __nv_bfloat16*)bias, C::kResidual ? (float*)Y : nullptr, ldy,
       (int)M, (int)N, (int)K);
   return mes_host::from_cuda(cudaGetLastError());
 }
 
 // Tile configuration for M > 64 tokens.  The environment variable MES_GEMM_CONFIG (read
-// once) selects among the compiled variants for tuning: 0 = 128 tokens / 4 dequant warps,
-// 1 = 128 tokens / 8 dequant warps, 2 = 256 tokens / 8 dequant warps; persistent with
-// double-buffered accumulators: 3 = 192 tokens, 4 smem / 4 TMEM stages; 4 = 192 tokens,
-// 7 / 4 stages; 5 = 128 tokens, 8 / 8 stages; A tile in shared memory: 6 = 256 tokens,
-// 4 stages (default: reading A from TMEM measured ~1.3x slower per MMA than from shared
-// memory for this shape); 7 = 192 tokens, 4 stages.
+// once) selects among the compiled variants for tuning: 0 = persistent, 256 tokens,
+// dequantised A in shared memory (default); 1 = persistent, 192 tokens, dequantised A in
+// TMEM (measured ~1.3x slower per MMA for this shape); 2 = one 256-token tile per CTA.
 int large_m_config() {
   static int cfg = [] {
     const char* v = getenv("MES_GEMM_CONFIG");
-    int c = v ? atoi(v) : 6;
-    return (c < 0 || c > 7) ? 6 : c;
+    int c = v ? atoi(v) : 0;
+    return (c < 0 || c > 2) ? 0 : c;
   }();
   return cfg;
 }
 
-template <bool kResidual>
+template <int EPI>
 int dispatch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
                   const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
                   int64_t N, int64_t K, cudaStream_t s) {
-  if (M <= 16) return launch_gemm<16, 6, kResidual, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-  if (M <= 32) return launch_gemm<32, 6, kResidual, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-  if (M <= 64) return launch_gemm<64, 6, kResidual, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  if (M <= 16) return launch_gemm<16, 6, EPI, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  if (M <= 32) return launch_gemm<32, 6, EPI, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  if (M <= 64) return launch_gemm<64, 6, EPI, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
   switch (large_m_config()) {
-    case 0: return launch_gemm<128, 4, kResidual, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-    case 2: return launch_gemm<256, 4, kResidual, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-    case 3: return launch_gemm_persistent<192, 4, 4, kResidual, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-    case 4: return launch_gemm_persistent<192, 7, 4, kResidual, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-    case 5: return launch_gemm_persistent<128, 8, 8, kResidual, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-    case 6: return launch_gemm_persistent<256, 4, 0, kResidual, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-    case 7: return launch_gemm_persistent<192, 4, 0, kResidual, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-    default: return launch_gemm<128, 4, kResidual, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+    case 1: return launch_gemm_persistent<192, 4, 4, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+    case 2: return launch_gemm<256, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+    default: return launch_gemm_persistent<256, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
   }
 }
 
+// Host checks shared by the GEMM entry points; returns -1 for an empty product (M == 0).
 int check_gemm_args(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
                     const void* scales, const void* Y, int64_t ldy, int64_t M, int64_t N,
-                    int64_t K, int group_size, int y_elem_align) {
+                    int64_t K, int group_size, int y_elem_align, int64_t y_cols) {
   if (M < 0 || N <= 0 || K <= 0 || N % kBN || K % kGroup || group_size != kGroup)
     return MES_ERR_INVALID;
   if (N > (1 << 30) || K > (1 << 30) || M > (1LL << 31) - 256) return MES_ERR_INVALID;
-  if (ldx < K || ldy < N || ldx % 8 || ldy % y_elem_align) return MES_ERR_INVALID;
+  if (ldx < K || ldy < y_cols || ldx % 8 || ldy % y_elem_align) return MES_ERR_INVALID;
   if (M == 0) return -1;
   if (!X || !qw || !qzeros || !scales || !Y) return MES_ERR_INVALID;
   return MES_OK;
@@ -816,11 +863,11 @@ extern "C" int mes_awq_gemm(const void* X, int64_t ldx, const int32_t* qweight_m
                             int64_t ldy, int64_t M, int64_t N, int64_t K, int group_size,
                             void* stream) {
   const int st = check_gemm_args(X, ldx, qweight_mes, qzeros, scales, Y, ldy, M, N, K,
-                                 group_size, 8);
+                                 group_size, 8, N);
   if (st != MES_OK) return st < 0 ? MES_OK : st;
   if (!aligned16(X) || !aligned16(Y) || !aligned16(qweight_mes)) return MES_ERR_ALIGN;
-  return dispatch_gemm<false>(X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K,
-                              (cudaStream_t)stream);
+  return dispatch_gemm<kEpiBf16>(X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K,
+                                 (cudaStream_t)stream);
 }
 
 extern "C" int mes_awq_gemm_residual(const void* X, int64_t ldx, const int32_t* qweight_mes,
@@ -828,10 +875,21 @@ extern "C" int mes_awq_gemm_residual(const void* X, int64_t ldx, const int32_t* 
                                      float* R, int64_t ldr, int64_t M, int64_t N, int64_t K,
                                      int group_size, void* stream) {
   const int st = check_gemm_args(X, ldx, qweight_mes, qzeros, scales, R, ldr, M, N, K,
-                                 group_size, 1);
+                                 group_size, 1, N);
   if (st != MES_OK) return st < 0 ? MES_OK : st;
   if (!aligned16(X) || !aligned16(qweight_mes) || (reinterpret_cast<uintptr_t>(R) & 3))
     return MES_ERR_ALIGN;
-  return dispatch_gemm<true>(X, ldx, qweight_mes, qzeros, scales, bias, R, ldr, M, N, K,
-                             (cudaStream_t)stream);
+  return dispatch_gemm<kEpiResidual>(X, ldx, qweight_mes, qzeros, scales, bias, R, ldr, M, N, K,
+                                     (cudaStream_t)stream);
+}
+
+extern "C" int mes_awq_gemm_silu(const void* X, int64_t ldx, const int32_t* qweight_mes,
+                                 const int32_t* qzeros, const void* scales, void* Y, int64_t ldy,
+                                 int64_t M, int64_t N, int64_t K, int group_size, void* stream) {
+  const int st = check_gemm_args(X, ldx, qweight_mes, qzeros, scales, Y, ldy, M, N, K,
+                                 group_size, 8, N / 2);
+  if (st != MES_OK) return st < 0 ? MES_OK : st;
+  if (!aligned16(X) || !aligned16(Y) || !aligned16(qweight_mes)) return MES_ERR_ALIGN;
+  return dispatch_gemm<kEpiSilu>(X, ldx, qweight_mes, qzeros, scales, nullptr, Y, ldy, M, N, K,
+                                 (cudaStream_t)stream);
 }

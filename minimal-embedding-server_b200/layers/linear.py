@@ -186,6 +186,36 @@ class MergedColumnParallelLinear(ColumnParallelLinear):
         offset = sum(self.output_sizes[:loaded_shard_id]) // tp
         size = self.output_sizes[loaded_shard_id] // tp
         self._load_out_range(param, loaded_weight, offset, size, self.tp_rank * size)
+        self._silu_pack = None
+
+    def process_weights_after_loading(self):
+        """Build the kernel layout the model will use: the gate/up-interleaved pack for the
+        fused SiLU GEMM when it applies (the plain layout is then built only on demand)."""
+        if self.supports_silu():
+            self._silu_pack = None
+            self._silu_pack = self._build_silu_pack()
+        else:
+            super().process_weights_after_loading()
+
+    def _build_silu_pack(self):
+        qw, qz, sc = _C.interleave_gate_up(self.qweight.data, self.qzeros.data, self.scales.data)
+        return (_C.awq_repack(qw), qz, sc)
+
+    def supports_silu(self) -> bool:
+        """Whether forward_silu applies: two equal halves, 64-aligned per rank, no bias."""
+        return (len(self.output_sizes) == 2 and self.output_sizes[0] == self.output_sizes[1]
+                and (self.output_size_per_partition // 2) % 64 == 0
+                and self.output_size_per_partition % 128 == 0 and self.bias is None)
+
+    def forward_silu(self, x: torch.Tensor) -> torch.Tensor:
+        """``SiluAndMul(self(x))`` as one GEMM: the epilogue multiplies silu(gate) by up
+        (``layers/activation.py:12-14``), so the [T, 2I] projection never reaches HBM."""
+        pack = getattr(self, "_silu_pack", None)
+        if pack is None or pack[0].device != self.qweight.device:
+            pack = self._silu_pack = self._build_silu_pack()
+        shape = x.shape
+        y = _C.awq_gemm_silu(x.reshape(-1, shape[-1]), *pack, group_size=self.group_size)
+        return y.view(*shape[:-1], y.shape[-1])
 
 
 class QKVParallelLinear(ColumnParallelLinear):

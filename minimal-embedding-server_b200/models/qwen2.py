@@ -114,7 +114,11 @@ class Qwen2MLP(nn.Module):
         return self.down_proj(self.act_fn(self.gate_up_proj(x)))
 
     def forward_residual(self, x, residual):
-        return self.down_proj.forward_residual(self.act_fn(self.gate_up_proj(x)), residual)
+        if self.gate_up_proj.supports_silu():
+            act = self.gate_up_proj.forward_silu(x)   # GEMM with SiLU-and-mul epilogue
+        else:
+            act = self.act_fn(self.gate_up_proj(x))
+        return self.down_proj.forward_residual(act, residual)
 
 
 def _attn_kwargs(model_config, qkv_bias: bool, qk_norm: bool) -> dict:
