@@ -122,68 +122,78 @@ __global__ void rmsnorm_kernel(const XT* x, const RT* residual, const uint4* __r
 }
 
 // ------------------------------ q/k RMSNorm + NeoX RoPE --------------------------------
-// 16 threads per (token, head): thread j holds elements 8j..8j+7 of the 128-wide head.
-// The rotate-half partner of thread j is j ^ 8.
-template <bool kNorm, bool kF32Cache>
-__global__ void qknorm_rope_kernel(bf162* __restrict__ qkv, int64_t ld, const int64_t* __restrict__ pos,
-                                   const void* __restrict__ cos_sin, int64_t max_pos,
-                                   const uint4* __restrict__ qw, const uint4* __restrict__ kw,
-                                   int64_t T, int Hq, int Hkv, float eps) {
-  const int nh = Hq + Hkv;
-  const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int64_t item = gid >> 4;  // (token, head)
-  const int j = threadIdx.x & 15;
-  const bool valid = item < T * nh;
-  const int64_t t = valid ? item / nh : 0;
-  const int h = valid ? (int)(item - t * nh) : 0;
-  uint4* rowp = reinterpret_cast<uint4*>(qkv + (t * ld) / 2) + h * 16 + j;
-  float f[8];
-  uint4 raw = valid ? *rowp : make_uint4(0, 0, 0, 0);
-  unpack8(raw, f);
-  if (kNorm) {
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float rs = rsqrtf(ss * (1.0f / 128.0f) + eps);
-    float wf[8];
-    unpack8((h < Hq ? qw : kw)[j], wf);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) f[i] = round_bf16(round_bf16(f[i] * rs) * wf[i]);
+// 16 threads per token: thread j owns elements 8j..8j+7 of every 128-wide head, so the
+// token's cos/sin values, position and norm weights are loaded once and reused for all of
+// its heads; heads are processed four at a time for memory-level parallelism.  The
+// rotate-half partner of thread j is j ^ 8.
+template <bool kF32Cache>
+__device__ __forceinline__ void load_cos_sin(const void* cos_sin, int64_t ps, int cj, float (&c)[8],
+                                             float (&s)[8]) {
+  if (kF32Cache) {
+    const float4* cs = reinterpret_cast<const float4*>(static_cast<const float*>(cos_sin) + ps * 128);
+    const float4 a = __ldg(cs + cj / 4), b = __ldg(cs + cj / 4 + 1);
+    const float4 d = __ldg(cs + 16 + cj / 4), e = __ldg(cs + 16 + cj / 4 + 1);
+    c[0] = a.x; c[1] = a.y; c[2] = a.z; c[3] = a.w; c[4] = b.x; c[5] = b.y; c[6] = b.z; c[7] = b.w;
+    s[0] = d.x; s[1] = d.y; s[2] = d.z; s[3] = d.w; s[4] = e.x; s[5] = e.y; s[6] = e.z; s[7] = e.w;
+  } else {
+    const uint4* cs = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(cos_sin) + ps * 128);
+    unpack8(__ldg(cs + cj / 8), c);
+    unpack8(__ldg(cs + 8 + cj / 8), s);
   }
-  float p[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = __shfl_xor_sync(0xffffffffu, f[i], 8);
+}
+
+template <bool kNorm, bool kF32Cache>
+__global__ void __launch_bounds__(256)
+qknorm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, const int64_t* __restrict__ pos,
+                   const void* __restrict__ cos_sin, int64_t max_pos, const uint4* __restrict__ qw,
+                   const uint4* __restrict__ kw, int T, int Hq, int Hkv, float eps) {
+  const int nh = Hq + Hkv;
+  const int t = blockIdx.x * 16 + (threadIdx.x >> 4);
+  const int j = threadIdx.x & 15;
+  const bool valid = t < T;
   int64_t ps = valid ? __ldg(pos + t) : 0;
   if (ps < 0 || ps >= max_pos) {
     if (valid && j == 0) atomicCAS(&g_err_elementwise, 0, MES_ERR_INVALID);
     ps = 0;
   }
-  const int cj = (j & 7) * 8;  // cos/sin column of this thread's first element
   float c[8], s[8];
-  if (kF32Cache) {
-    const float4* cs = reinterpret_cast<const float4*>(
-        static_cast<const float*>(cos_sin) + ps * 128);
-    float4 a = __ldg(cs + cj / 4), b = __ldg(cs + cj / 4 + 1);
-    float4 d = __ldg(cs + 16 + cj / 4), e = __ldg(cs + 16 + cj / 4 + 1);
-    c[0] = a.x; c[1] = a.y; c[2] = a.z; c[3] = a.w; c[4] = b.x; c[5] = b.y; c[6] = b.z; c[7] = b.w;
-    s[0] = d.x; s[1] = d.y; s[2] = d.z; s[3] = d.w; s[4] = e.x; s[5] = e.y; s[6] = e.z; s[7] = e.w;
-  } else {
-    const uint4* cs = reinterpret_cast<const uint4*>(
-        static_cast<const __nv_bfloat16*>(cos_sin) + ps * 128);
-    unpack8(__ldg(cs + cj / 8), c);
-    unpack8(__ldg(cs + 8 + cj / 8), s);
+  load_cos_sin<kF32Cache>(cos_sin, ps, (j & 7) * 8, c, s);
+  float wq[8], wk[8];
+  if (kNorm) {
+    unpack8(Hq > 0 ? __ldg(qw + j) : make_uint4(0, 0, 0, 0), wq);
+    unpack8(Hkv > 0 ? __ldg(kw + j) : make_uint4(0, 0, 0, 0), wk);
   }
-  float o[8];
-  if (j < 8) {
+  uint4* row = reinterpret_cast<uint4*>(qkv + (int64_t)(valid ? t : 0) * ld) + j;
+  for (int h0 = 0; h0 < nh; h0 += 4) {
+    uint4 raw[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = f[i] * c[i] - p[i] * s[i];
-  } else {
+    for (int u = 0; u < 4; ++u)
+      raw[u] = (valid && h0 + u < nh) ? row[(h0 + u) * 16] : make_uint4(0, 0, 0, 0);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = f[i] * c[i] + p[i] * s[i];
+    for (int u = 0; u < 4; ++u) {
+      if (h0 + u >= nh) break;  // uniform across the warp
+      float f[8];
+      unpack8(raw[u], f);
+      if (kNorm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float rs = rsqrtf(ss * (1.0f / 128.0f) + eps);
+        const bool is_q = h0 + u < Hq;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = round_bf16(round_bf16(f[i] * rs) * (is_q ? wq[i] : wk[i]));
+      }
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float p = __shfl_xor_sync(0xffffffffu, f[i], 8);
+        o[i] = j < 8 ? f[i] * c[i] - p * s[i] : f[i] * c[i] + p * s[i];
+      }
+      if (valid) row[(h0 + u) * 16] = pack8(o);
+    }
   }
-  if (valid) *rowp = pack8(o);
 }
 
 // ------------------------------------ SiLU-and-mul -------------------------------------
@@ -419,24 +429,22 @@ extern "C" int mes_qknorm_rope(void* qkv, int64_t ld, const int64_t* positions,
   if (apply_norm && ((Hq > 0 && !q_w) || (Hkv > 0 && !k_w))) return MES_ERR_INVALID;
   if (!aligned16(qkv) || !aligned16(cos_sin) || (apply_norm && (!aligned16(q_w) || !aligned16(k_w))))
     return MES_ERR_ALIGN;
-  const int64_t threads = T * (Hq + Hkv) * 16;
-  const int64_t blocks = (threads + 255) / 256;
+  if (T > 0x7fffffffLL - 16) return MES_ERR_INVALID;
+  const unsigned blocks = (unsigned)((T + 15) / 16);
   cudaStream_t s = (cudaStream_t)stream;
-  bf162* p = (bf162*)qkv;
+  __nv_bfloat16* p = (__nv_bfloat16*)qkv;
+  const uint4* qwp = (const uint4*)q_w;
+  const uint4* kwp = (const uint4*)k_w;
   if (apply_norm) {
     if (cos_sin_f32)
-      qknorm_rope_kernel<true, true><<<(unsigned)blocks, 256, 0, s>>>(
-          p, ld, positions, cos_sin, max_pos, (const uint4*)q_w, (const uint4*)k_w, T, Hq, Hkv, eps);
+      qknorm_rope_kernel<true, true><<<blocks, 256, 0, s>>>(p, ld, positions, cos_sin, max_pos, qwp, kwp, (int)T, Hq, Hkv, eps);
     else
-      qknorm_rope_kernel<true, false><<<(unsigned)blocks, 256, 0, s>>>(
-          p, ld, positions, cos_sin, max_pos, (const uint4*)q_w, (const uint4*)k_w, T, Hq, Hkv, eps);
+      qknorm_rope_kernel<true, false><<<blocks, 256, 0, s>>>(p, ld, positions, cos_sin, max_pos, qwp, kwp, (int)T, Hq, Hkv, eps);
   } else {
     if (cos_sin_f32)
-      qknorm_rope_kernel<false, true><<<(unsigned)blocks, 256, 0, s>>>(
-          p, ld, positions, cos_sin, max_pos, nullptr, nullptr, T, Hq, Hkv, eps);
+      qknorm_rope_kernel<false, true><<<blocks, 256, 0, s>>>(p, ld, positions, cos_sin, max_pos, nullptr, nullptr, (int)T, Hq, Hkv, eps);
     else
-      qknorm_rope_kernel<false, false><<<(unsigned)blocks, 256, 0, s>>>(
-          p, ld, positions, cos_sin, max_pos, nullptr, nullptr, T, Hq, Hkv, eps);
+      qknorm_rope_kernel<false, false><<<blocks, 256, 0, s>>>(p, ld, positions, cos_sin, max_pos, nullptr, nullptr, (int)T, Hq, Hkv, eps);
   }
   return mes_host::from_cuda(cudaGetLastError());
 }
