@@ -318,6 +318,424 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
   }
 }
 
+// =========================================================================================
+// Head-pair kernel (query heads per KV head even): two query heads of one KV group share
+// every K/V tile.  Per item (sequence, 128-row query tile, head pair):
+//   * warp 8 (TMA) loads both Q tiles (64 KB) and, for key tiles 0 .. qtile, K and V into
+//     separate 2-stage rings;
+//   * warp 9 (one thread) issues, in this order,
+//       S0_0, S1_0, { PV0_j, S0_{j+1}, PV1_j, S1_{j+1} } for j = 0 .. qtile,
+//     so the tensor core runs tile 1's MMAs while warpgroup 0 runs the softmax of tile 0
+//     and the other way round;
+//   * warps 0-3 / 4-7 run the online softmax of head 0 / head 1 of the pair (one query row
+//     per thread), write P (bf16) over the first 64 columns of their own S buffer, rescale
+//     O in TMEM when the running maximum grew by more than 2^8, and store O / l at the end.
+// TMEM: S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512); P_b aliases S_b.
+// tcgen05.mma operations issued by one thread execute in issue order, so S_b(j+1), issued
+// after PV_b(j), overwrites P_b(j) only after PV_b(j) has read it, and the commit that
+// signals S_b(j+1) also covers PV_b(j): when warpgroup b sees S_b(j+1), O_b holds every
+// P_b(i) V_i for i <= j and no MMA writes O_b until warpgroup b publishes P_b(j+1).
+//
+// exp2 runs on two units: the special-function unit (ex2.approx) and, for kPolyPairs of
+// every 8 element pairs, the FMA pipe with 2^x = 2^n * q(x - n), n = round(x), and q a
+// degree-3 polynomial for 2^f on [-1/2, 1/2] fitted for minimum maximum relative error
+// (Lawson's iteratively reweighted least squares; max relative error 7.5e-5, against the
+// 2^-9 relative rounding of P to bf16).  Packed f32x2 FMA / add halve the issue count of
+// the element-wise work.
+constexpr int kPThreads = 384;  // warps 0-7 softmax, 8 TMA, 9 MMA, 10-11 idle
+// Register split (setmaxnreg acts on whole warpgroups): softmax warpgroups grow to
+// kSoftmaxRegs, warpgroup 2 shrinks to kOtherRegs.  The host launches the kernel only when
+// the registers it was compiled for cover the split (otherwise setmaxnreg.inc would wait).
+constexpr int kSoftmaxRegs = 200;
+constexpr int kOtherRegs = 104;
+constexpr int kPOffQ = 0;                                   // Q0 | Q1, 2 x 32 KB
+constexpr int kPOffK = kPOffQ + 2 * kQBytes;
+constexpr int kPOffV = kPOffK + kKVStages * kKVBytes;
+constexpr int kPOffBar = kPOffV + kKVStages * kKVBytes;
+constexpr int kPSmem = kPOffBar + 256 + 1024;
+static_assert(kPSmem <= 232448, "shared memory");
+
+__device__ __forceinline__ uint64_t f2_bits(float2 v) {
+  return (uint64_t)__float_as_uint(v.x) | ((uint64_t)__float_as_uint(v.y) << 32);
+}
+__device__ __forceinline__ float2 bits_f2(uint64_t b) {
+  return make_float2(__uint_as_float((uint32_t)b), __uint_as_float((uint32_t)(b >> 32)));
+}
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float ex2_sfu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// 2^x for a pair on the FMA pipe (x <= 2^22); inputs below -126 give about 2^-126.
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 t = fadd2(x, make_float2(kRound, kRound));
+  const float2 n = fadd2(t, make_float2(-kRound, -kRound));
+  const float2 f = fadd2(x, make_float2(-n.x, -n.y));
+  float2 q = ffma2(make_float2(0x1.c3f76p-5f, 0x1.c3f76p-5f), f, make_float2(0x1.f0de1cp-3f, 0x1.f0de1cp-3f));
+  q = ffma2(q, f, make_float2(0x1.62f31ap-1f, 0x1.62f31ap-1f));
+  q = ffma2(q, f, make_float2(0x1.fff692p-1f, 0x1.fff692p-1f));
+  // The low bits of t hold n; shifting them into the exponent field scales q by 2^n.
+  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
+}
+
+// Work index of the k-th item of CTA b: rows of the descending-cost list are dealt out
+// left to right, then right to left, so every CTA's total cost stays close to the mean.
+__device__ __forceinline__ int snake(int k, int b, int G) {
+  return k * G + ((k & 1) ? (G - 1 - b) : b);
+}
+
+template <int kPolyPairs>
+__global__ void __launch_bounds__(kPThreads, 1)
+varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
+                             __nv_bfloat16* __restrict__ out, const int* __restrict__ hdr,
+                             const int* __restrict__ cu, const int2* __restrict__ items, int Hq,
+                             int Hkv, float scale_log2) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* qs = smem + kPOffQ;
+  uint8_t* ks = smem + kPOffK;
+  uint8_t* vs = smem + kPOffV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPOffBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;    // [kKVStages]
+  uint64_t* k_empty = bars + 4;   // [kKVStages]
+  uint64_t* v_full = bars + 6;    // [kKVStages]
+  uint64_t* v_empty = bars + 8;   // [kKVStages]
+  uint64_t* s_full = bars + 10;   // [2] per head of the pair
+  uint64_t* p_full = bars + 12;   // [2]
+  uint64_t* o_full = bars + 14;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = mes::warp_id(), lane = mes::lane_id();
+  const int npairs = Hq / 2;
+  const int num_work = hdr[1] * npairs;
+  const int rep = Hq / Hkv;
+
+  if (threadIdx.x == 0) {
+    mes::mbar_init(q_full, 1);
+    mes::mbar_init(q_empty, 1);
+    for (int s = 0; s < kKVStages; ++s) {
+      mes::mbar_init(&k_full[s], 1);
+      mes::mbar_init(&k_empty[s], 1);
+      mes::mbar_init(&v_full[s], 1);
+      mes::mbar_init(&v_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mes::mbar_init(&s_full[b], 1);
+      mes::mbar_init(&p_full[b], 4);
+      mes::mbar_init(&o_full[b], 1);
+    }
+    *abort_flag = 0;
+    mes::fence_barrier_init();
+  }
+  if (warp == 8 && lane == 0) mes::tma_prefetch_desc(&map_qkv);
+  if (warp == 9) {
+    __syncwarp();
+    mes::tmem_alloc(tmem_slot, kTmemCols);
+    mes::tmem_relinquish();
+  }
+  mes::tc_fence_before();
+  __syncthreads();
+  mes::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= 8) {
+   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kOtherRegs));
+   if (warp == 8) {
+    // ------------------------------------ TMA ----------------------------------------
+    if (lane == 0) {
+      int n_item = 0, kt = 0, vt = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < num_work && ok; w = snake(++n_item, blockIdx.x, gridDim.x)) {
+        const int2 it = items[w / npairs];
+        const int h0 = 2 * (w % npairs), g = h0 / rep;
+        const int start = cu[it.x];
+        const int q0 = start + it.y * kTile;
+        if (n_item > 0 && !mes::mbar_wait(q_empty, (n_item - 1) & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) {
+          ok = false;
+          break;
+        }
+        mes::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          mes::tma_load_2d(qs + c * (kQBytes / 2), &map_qkv, q_full, h0 * kD + c * 64, q0);
+        const int kcol = (Hq + g) * kD, vcol = (Hq + Hkv + g) * kD;
+        for (int j = 0; j <= it.y; ++j, ++kt, ++vt) {
+          const int k0 = start + j * kTile;
+          const int ks_ = kt % kKVStages, vs_ = vt % kKVStages;
+          if (kt >= kKVStages &&
+              !mes::mbar_wait(&k_empty[ks_], ((kt / kKVStages) & 1) ^ 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          uint8_t* kd = ks + ks_ * kKVBytes;
+          mes::mbar_arrive_expect_tx(&k_full[ks_], kKVBytes);
+          mes::tma_load_2d(kd, &map_qkv, &k_full[ks_], kcol, k0);
+          mes::tma_load_2d(kd + kKVBytes / 2, &map_qkv, &k_full[ks_], kcol + 64, k0);
+          if (vt >= kKVStages &&
+              !mes::mbar_wait(&v_empty[vs_], ((vt / kKVStages) & 1) ^ 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          uint8_t* vd = vs + vs_ * kKVBytes;
+          mes::mbar_arrive_expect_tx(&v_full[vs_], kKVBytes);
+          mes::tma_load_2d(vd, &map_qkv, &v_full[vs_], vcol, k0);
+          mes::tma_load_2d(vd + kKVBytes / 2, &map_qkv, &v_full[vs_], vcol + 64, k0);
+        }
+      }
+      if (!ok) {
+        // Give copies already in flight time to land before the CTA exits.
+        const uint64_t t = mes::globaltimer_ns();
+        while (mes::globaltimer_ns() - t < 1000000ull) {
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 9) {
+    // ------------------------------------ MMA ----------------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = mes::idesc_bf16_f32(kTile, kTile, false);
+      constexpr uint32_t idesc_o = mes::idesc_bf16_f32(kTile, kD, true);
+      // Descriptors differ only in the start-address field (bits [0,14), address >> 4), and
+      // every operand lies below 256 KB, so offsets are added to a base descriptor.
+      const uint64_t dq = mes::smem_desc_sw128(mes::smem_u32(qs), 16, 1024);
+      const uint64_t dk = mes::smem_desc_sw128(mes::smem_u32(ks), 16, 1024);
+      const uint64_t dv = mes::smem_desc_sw128(mes::smem_u32(vs), kKVBytes / 2, 1024);
+      auto issue_s = [&](int b, int st) {
+        const uint64_t da = dq + (uint32_t)(b * (kQBytes >> 4));
+        const uint64_t db = dk + (uint32_t)(st * (kKVBytes >> 4));
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = ((kk >> 2) * (kQBytes / 2) + (kk & 3) * 32) >> 4;
+          mes::mma_ss(tmem + b * 128, da + off, db + off, idesc_s, kk != 0);
+        }
+      };
+      auto issue_pv = [&](int b, int st, bool acc) {
+        // V tile: keys are the MMA's K; 128-byte rows of 64 head-dim elements, the second
+        // 64-column box is the next MN block (LBO = 16 KB), 8-row atoms 1 KB apart (SBO).
+        const uint64_t dvs = dv + (uint32_t)(st * (kKVBytes >> 4));
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          mes::mma_ts(tmem + 256 + b * 128, tmem + b * 128 + kk * 8, dvs + (uint32_t)(kk * 128),
+                      idesc_o, acc || kk > 0);
+      };
+      int n_item = 0, kt = 0, vt = 0, pt = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < num_work && ok; w = snake(++n_item, blockIdx.x, gridDim.x)) {
+        const int nt = items[w / npairs].y + 1;
+        if (!mes::mbar_wait(q_full, n_item & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
+        if (!mes::mbar_wait(&k_full[kt % kKVStages], (kt / kKVStages) & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
+        mes::tc_fence_after();
+        issue_s(0, kt % kKVStages);
+        mes::tc_commit(&s_full[0]);
+        issue_s(1, kt % kKVStages);
+        mes::tc_commit(&s_full[1]);
+        mes::tc_commit(&k_empty[kt % kKVStages]);
+        ++kt;
+        if (nt == 1) mes::tc_commit(q_empty);
+        for (int j = 0; j < nt; ++j, ++vt, ++pt) {
+          const int vst = vt % kKVStages;
+          if (!mes::mbar_wait(&p_full[0], pt & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
+          if (!mes::mbar_wait(&v_full[vst], (vt / kKVStages) & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
+          mes::tc_fence_after();
+          issue_pv(0, vst, j > 0);
+          if (j == nt - 1) mes::tc_commit(&o_full[0]);
+          const bool more = j + 1 < nt;
+          if (more) {
+            if (!mes::mbar_wait(&k_full[kt % kKVStages], (kt / kKVStages) & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
+            mes::tc_fence_after();
+            issue_s(0, kt % kKVStages);
+            mes::tc_commit(&s_full[0]);
+          }
+          if (!mes::mbar_wait(&p_full[1], pt & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
+          mes::tc_fence_after();
+          issue_pv(1, vst, j > 0);
+          mes::tc_commit(&v_empty[vst]);
+          if (j == nt - 1) mes::tc_commit(&o_full[1]);
+          if (more) {
+            issue_s(1, kt % kKVStages);
+            mes::tc_commit(&s_full[1]);
+            mes::tc_commit(&k_empty[kt % kKVStages]);
+            ++kt;
+            if (j + 1 == nt - 1) mes::tc_commit(q_empty);
+          }
+        }
+      }
+      if (!ok) {
+        const uint64_t t = mes::globaltimer_ns();
+        while (mes::globaltimer_ns() - t < 1000000ull) {
+        }
+      }
+    }
+    __syncwarp();
+   }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
+    // ---------------------------------- softmax -------------------------------------
+    const int b = warp >> 2;           // head of the pair
+    const int r = (warp & 3) * 32 + lane;  // query row within the tile
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + lane_off + b * 128;
+    const uint32_t t_o = tmem + lane_off + 256 + b * 128;
+    const float2 sc2 = make_float2(scale_log2, scale_log2);
+    int n_item = 0, pt = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < num_work && ok; w = snake(++n_item, blockIdx.x, gridDim.x)) {
+      const int2 item = items[w / npairs];
+      const int h = 2 * (w % npairs) + b;
+      const int start = cu[item.x], len = cu[item.x + 1] - start;
+      const int nt = item.y + 1;
+      float m = 0.f, l = 0.f;
+      for (int j = 0; j < nt; ++j, ++pt) {
+        if (!mes::mbar_wait_warp(&s_full[b], pt & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
+        mes::tc_fence_after();
+        float s[kTile];
+        {
+          uint32_t v0[32], v1[32], v2[32], v3[32];
+          mes::tmem_ld32(t_s + 0, v0);
+          mes::tmem_ld32(t_s + 32, v1);
+          mes::tmem_ld32(t_s + 64, v2);
+          mes::tmem_ld32(t_s + 96, v3);
+          mes::tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            s[c] = __uint_as_float(v0[c]);
+            s[32 + c] = __uint_as_float(v1[c]);
+            s[64 + c] = __uint_as_float(v2[c]);
+            s[96 + c] = __uint_as_float(v3[c]);
+          }
+        }
+        // Causal mask on the diagonal tile: key c is visible to row r iff c <= r.
+        if (j == nt - 1) {
+#pragma unroll
+          for (int c = 0; c < kTile; ++c)
+            if (c > r) s[c] = -INFINITY;
+        }
+        float mq[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mq[u] = fmaxf(s[2 * u], s[2 * u + 1]);
+#pragma unroll
+        for (int c = 8; c < kTile; c += 8)
+#pragma unroll
+          for (int u = 0; u < 4; ++u) mq[u] = fmax3(mq[u], s[c + 2 * u], s[c + 2 * u + 1]);
+        float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale_log2;
+        // Lazy rescale: move to the new maximum only when it grew by more than 2^8 (the
+        // decision is warp-uniform because tcgen05.ld/st are warp-collective; rows whose
+        // maximum did not grow scale by 1).  O_b is rescaled after P_b is written, when
+        // the S registers are dead; no MMA touches O_b before P_b is published.
+        float f = 1.0f;
+        bool rescale = false;
+        if (j == 0) {
+          m = mx;
+        } else if (__any_sync(0xffffffffu, mx > m + 8.0f)) {
+          const float mn = fmaxf(m, mx);
+          f = ex2_sfu(m - mn);
+          l *= f;
+          m = mn;
+          rescale = true;
+        }
+        const float2 nm2 = make_float2(-m, -m);
+        float2 sum2[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) sum2[u] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int c = q4 * 32 + 2 * i;
+            const float2 x = ffma2(make_float2(s[c], s[c + 1]), sc2, nm2);
+            float2 p;
+            if ((i & 7) < kPolyPairs) {
+              p = ex2_poly2(x);
+            } else {
+              p.x = ex2_sfu(x.x);
+              p.y = ex2_sfu(x.y);
+            }
+            sum2[i & 3] = fadd2(sum2[i & 3], p);
+            pk[i] = mes::pack_bf16x2(p.x, p.y);
+          }
+          mes::tmem_st16(t_s + q4 * 16, pk);
+        }
+        const float2 s01 = fadd2(sum2[0], sum2[1]), s23 = fadd2(sum2[2], sum2[3]);
+        l += (s01.x + s23.x) + (s01.y + s23.y);
+        if (rescale) {
+#pragma unroll 1
+          for (int c = 0; c < kD; c += 32) {
+            uint32_t v[32];
+            mes::tmem_ld32(t_o + c, v);
+            mes::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * f);
+            mes::tmem_st32(t_o + c, v);
+          }
+        }
+        mes::tmem_wait_st();
+        mes::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mes::mbar_arrive(&p_full[b]);
+        __syncwarp();
+      }
+      if (!ok) break;
+      // Epilogue: O / l for this item's rows.
+      if (!mes::mbar_wait_warp(&o_full[b], n_item & 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
+      mes::tc_fence_after();
+      const int row_in_seq = item.y * kTile + r;
+      const bool valid = row_in_seq < len;
+      const float inv = 1.0f / l;
+      uint4* dst = reinterpret_cast<uint4*>(out + ((int64_t)(start + row_in_seq) * Hq + h) * kD);
+#pragma unroll 1
+      for (int c = 0; c < kD; c += 32) {
+        uint32_t v[32];
+        mes::tmem_ld32(t_o + c, v);
+        mes::tmem_wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 o;
+            o.x = mes::pack_bf16x2(__uint_as_float(v[i + 0]) * inv, __uint_as_float(v[i + 1]) * inv);
+            o.y = mes::pack_bf16x2(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
+            o.z = mes::pack_bf16x2(__uint_as_float(v[i + 4]) * inv, __uint_as_float(v[i + 5]) * inv);
+            o.w = mes::pack_bf16x2(__uint_as_float(v[i + 6]) * inv, __uint_as_float(v[i + 7]) * inv);
+            dst[(c + i) / 8] = o;
+          }
+        }
+      }
+      mes::tc_fence_before();
+    }
+  }
+
+  mes::tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    mes::tc_fence_after();
+    mes::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 }  // namespace
 
 extern "C" int mes_attention_take_error(int* code) {
@@ -327,6 +745,26 @@ extern "C" int mes_attention_take_error(int* code) {
   e = cudaMemcpyToSymbol(g_err_attn, &zero, sizeof(int));
   *code = v;
   return mes_host::from_cuda(e);
+}
+
+// Element pairs (of every 8) whose exp2 runs on the FMA pipe in the head-pair kernel;
+// MES_ATTN_POLY in {0, 2, 3, 4} overrides the default for measurements.
+static int poly_pairs() {
+  static const int v = [] {
+    const char* e = getenv("MES_ATTN_POLY");
+    const int x = e ? atoi(e) : 0;
+    return (x == 2 || x == 3 || x == 4) ? x : 0;
+  }();
+  return v;
+}
+
+// The head-pair kernel's register split must fit in what each SM sub-partition holds for
+// the CTA at launch: three warps per sub-partition, one of them shrinking.
+template <typename K>
+static bool pair_kernel_registers_fit(K kern) {
+  cudaFuncAttributes a;
+  if (cudaFuncGetAttributes(&a, kern) != cudaSuccess) return false;
+  return 3 * a.numRegs >= 2 * kSoftmaxRegs + kOtherRegs && a.maxThreadsPerBlock >= kPThreads;
 }
 
 // Workspace layout is defined next to mes_varlen_schedule (elementwise.cu).
@@ -344,14 +782,29 @@ extern "C" int mes_varlen_attention(const void* qkv, int64_t ld, void* out, cons
   if (!mes_host::make_map_2d(&map, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, ld, ld, kTile, 64,
                              CU_TENSOR_MAP_SWIZZLE_128B))
     return MES_ERR_INVALID;
-  cudaError_t e = cudaFuncSetAttribute(varlen_attention_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-  if (e != cudaSuccess) return MES_ERR_CUDA;
   const char* ws = static_cast<const char*>(workspace);
   const int64_t items_off = ((256 + 4 * (T + 1)) + 255) & ~int64_t(255);
   const int grid = mes_host::sm_count();
-  varlen_attention_kernel<<<grid, kThreads, kSmem, (cudaStream_t)stream>>>(
+  const float scale_log2 = scale * 1.4426950408889634f;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int poly = poly_pairs();
+  auto kern = poly == 2   ? varlen_attention_pair_kernel<2>
+              : poly == 3 ? varlen_attention_pair_kernel<3>
+              : poly == 4 ? varlen_attention_pair_kernel<4>
+                          : varlen_attention_pair_kernel<0>;
+  if ((Hq / Hkv) % 2 == 0 && pair_kernel_registers_fit(kern)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
+    if (e != cudaSuccess) return MES_ERR_CUDA;
+    kern<<<grid, kPThreads, kPSmem, s>>>(map, (__nv_bfloat16*)out, (const int*)ws,
+                                         (const int*)(ws + 256), (const int2*)(ws + items_off),
+                                         Hq, Hkv, scale_log2);
+    return mes_host::from_cuda(cudaGetLastError());
+  }
+  cudaError_t e = cudaFuncSetAttribute(varlen_attention_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  if (e != cudaSuccess) return MES_ERR_CUDA;
+  varlen_attention_kernel<<<grid, kThreads, kSmem, s>>>(
       map, (__nv_bfloat16*)out, (const int*)ws, (const int*)(ws + 256), (const int2*)(ws + items_off),
-      Hq, Hkv, scale * 1.4426950408889634f);
+      Hq, Hkv, scale_log2);
   return mes_host::from_cuda(cudaGetLastError());
 }
