@@ -122,10 +122,11 @@ __global__ void rmsnorm_kernel(const XT* x, const RT* residual, const uint4* __r
 }
 
 // ------------------------------ q/k RMSNorm + NeoX RoPE --------------------------------
-// 16 threads per token: thread j owns elements 8j..8j+7 of every 128-wide head, so the
-// token's cos/sin values, position and norm weights are loaded once and reused for all of
-// its heads; heads are processed four at a time for memory-level parallelism.  The
-// rotate-half partner of thread j is j ^ 8.
+// 16 threads per (token, group of 4 heads): thread j owns elements 8j..8j+7 of each 128-wide
+// head, so the token's cos/sin values and the norm weights are loaded once per 4 heads and
+// the four heads' loads are in flight together.  Units are token-major, so a block covers
+// consecutive kilobytes of the packed qkv rows; the small units keep the grid at several
+// waves of the GPU.  The rotate-half partner of thread j is j ^ 8.
 template <bool kF32Cache>
 __device__ __forceinline__ void load_cos_sin(const void* cos_sin, int64_t ps, int cj, float (&c)[8],
                                              float (&s)[8]) {
@@ -148,51 +149,53 @@ qknorm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, const int64_t* _
                    const void* __restrict__ cos_sin, int64_t max_pos, const uint4* __restrict__ qw,
                    const uint4* __restrict__ kw, int T, int Hq, int Hkv, float eps) {
   const int nh = Hq + Hkv;
-  const int t = blockIdx.x * 16 + (threadIdx.x >> 4);
+  const int ngroups = (nh + 3) >> 2;
+  const int unit = blockIdx.x * 16 + (threadIdx.x >> 4);
   const int j = threadIdx.x & 15;
-  const bool valid = t < T;
+  const bool valid = unit < T * ngroups;
+  const int t = valid ? unit / ngroups : 0;
+  const int h0 = (unit - t * ngroups) * 4;
   int64_t ps = valid ? __ldg(pos + t) : 0;
   if (ps < 0 || ps >= max_pos) {
-    if (valid && j == 0) atomicCAS(&g_err_elementwise, 0, MES_ERR_INVALID);
+    if (valid && j == 0 && h0 == 0) atomicCAS(&g_err_elementwise, 0, MES_ERR_INVALID);
     ps = 0;
   }
   float c[8], s[8];
   load_cos_sin<kF32Cache>(cos_sin, ps, (j & 7) * 8, c, s);
   float wq[8], wk[8];
   if (kNorm) {
-    unpack8(Hq > 0 ? __ldg(qw + j) : make_uint4(0, 0, 0, 0), wq);
-    unpack8(Hkv > 0 ? __ldg(kw + j) : make_uint4(0, 0, 0, 0), wk);
+    unpack8(h0 < Hq ? __ldg(qw + j) : make_uint4(0, 0, 0, 0), wq);
+    unpack8(Hkv > 0 && h0 + 4 > Hq ? __ldg(kw + j) : make_uint4(0, 0, 0, 0), wk);
   }
-  uint4* row = reinterpret_cast<uint4*>(qkv + (int64_t)(valid ? t : 0) * ld) + j;
-  for (int h0 = 0; h0 < nh; h0 += 4) {
-    uint4 raw[4];
+  uint4* row = reinterpret_cast<uint4*>(qkv + (int64_t)t * ld) + h0 * 16 + j;
+  uint4 raw[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
-      raw[u] = (valid && h0 + u < nh) ? row[(h0 + u) * 16] : make_uint4(0, 0, 0, 0);
+  for (int u = 0; u < 4; ++u)
+    raw[u] = (valid && h0 + u < nh) ? row[u * 16] : make_uint4(0, 0, 0, 0);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (h0 + u >= nh) break;  // uniform across the warp
-      float f[8];
-      unpack8(raw[u], f);
-      if (kNorm) {
-        float ss = 0.f;
+  for (int u = 0; u < 4; ++u) {
+    // Every lane runs all four heads (the two units of a warp may differ in head count and
+    // the shuffles use the full mask); heads past the end compute on zeros and store nothing.
+    float f[8];
+    unpack8(raw[u], f);
+    if (kNorm) {
+      float ss = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float rs = rsqrtf(ss * (1.0f / 128.0f) + eps);
-        const bool is_q = h0 + u < Hq;
+      for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rs = rsqrtf(ss * (1.0f / 128.0f) + eps);
+      const bool is_q = h0 + u < Hq;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] = round_bf16(round_bf16(f[i] * rs) * (is_q ? wq[i] : wk[i]));
-      }
-      float o[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float p = __shfl_xor_sync(0xffffffffu, f[i], 8);
-        o[i] = j < 8 ? f[i] * c[i] - p * s[i] : f[i] * c[i] + p * s[i];
-      }
-      if (valid) row[(h0 + u) * 16] = pack8(o);
+      for (int i = 0; i < 8; ++i) f[i] = round_bf16(round_bf16(f[i] * rs) * (is_q ? wq[i] : wk[i]));
     }
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float p = __shfl_xor_sync(0xffffffffu, f[i], 8);
+      o[i] = j < 8 ? f[i] * c[i] - p * s[i] : f[i] * c[i] + p * s[i];
+    }
+    if (valid && h0 + u < nh) row[u * 16] = pack8(o);
   }
 }
 
@@ -423,14 +426,15 @@ extern "C" int mes_qknorm_rope(void* qkv, int64_t ld, const int64_t* positions,
                                const void* q_w, const void* k_w, int64_t T, int Hq, int Hkv,
                                int D, float eps, int apply_norm, void* stream) {
   if (D != 128 || T < 0 || Hq < 0 || Hkv < 0 || Hq + Hkv == 0 || max_pos <= 0) return MES_ERR_INVALID;
-  if (ld < (int64_t)(Hq + Hkv) * D || ld % 8) return MES_ERR_INVALID;
+  if (ld < ((int64_t)Hq + Hkv) * D || ld % 8) return MES_ERR_INVALID;
   if (T == 0) return MES_OK;
   if (!qkv || !positions || !cos_sin) return MES_ERR_INVALID;
   if (apply_norm && ((Hq > 0 && !q_w) || (Hkv > 0 && !k_w))) return MES_ERR_INVALID;
   if (!aligned16(qkv) || !aligned16(cos_sin) || (apply_norm && (!aligned16(q_w) || !aligned16(k_w))))
     return MES_ERR_ALIGN;
-  if (T > 0x7fffffffLL - 16) return MES_ERR_INVALID;
-  const unsigned blocks = (unsigned)((T + 15) / 16);
+  const int64_t units = T * (((int64_t)Hq + Hkv + 3) / 4);
+  if (units > 0x7fffffffLL - 16) return MES_ERR_INVALID;
+  const unsigned blocks = (unsigned)((units + 15) / 16);
   cudaStream_t s = (cudaStream_t)stream;
   __nv_bfloat16* p = (__nv_bfloat16*)qkv;
   const uint4* qwp = (const uint4*)q_w;

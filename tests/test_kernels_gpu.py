@@ -125,11 +125,12 @@ def test_rmsnorm_and_add_rmsnorm(rows, H):
 
 # ------------------------------------------------------------------------------ rope
 @pytest.mark.parametrize("norm,f32cache", [(True, False), (False, False), (True, True)])
-def test_qknorm_rope(norm, f32cache):
-    T, Hq, Hkv, D = 300, 16, 8, 128
+@pytest.mark.parametrize("T,Hq,Hkv", [(300, 16, 8), (77, 12, 2), (5, 2, 1)])
+def test_qknorm_rope(norm, f32cache, T, Hq, Hkv):
+    D = 128
     g = torch.Generator().manual_seed(3)
     qkv = bf16(torch.randn(T, (Hq + 2 * Hkv) * D, generator=g))
-    positions = torch.cat([torch.arange(100), torch.arange(150), torch.arange(50) + 4000])
+    positions = torch.cat([torch.arange(100), torch.arange(150), torch.arange(50) + 4000])[:T]
     cache = ops.rope_cos_sin_cache(D, 8192, 1e6)
     cache = cache if f32cache else bf16(cache)
     qw = bf16(1 + 0.1 * torch.randn(D, generator=g))
