@@ -781,15 +781,35 @@ int launch_gemm_persistent(const void* X, int64_t ldx, const int32_t* qw, const 
   return mes_host::from_cuda(cudaGetLastError());
 }
 
+// Token-tile width of the persistent kernel for an M x N product.  Every CTA walks
+// ceil(tiles / SMs) tiles at most, so the launch takes about that many tile times; a tile's
+// time grows with its width plus a fixed per-tile cost (the pipeline fill and the
+// accumulator hand-over), worth about 32 tokens.  The width that minimises
+// waves x (width + 32) is taken, the wider one on ties; e.g. N = 1024, M = 20000 on 148
+// SMs: 256 -> 632 tiles, 5 waves; 224 -> 720 tiles, 5 waves of shorter tiles.
+int persistent_tile_tokens(int64_t M, int64_t N) {
+  const int64_t sms = mes_host::sm_count();
+  const int widths[3] = {256, 224, 192};
+  int best = 256;
+  int64_t best_cost = INT64_MAX;
+  for (int w : widths) {
+    const int64_t tiles = (N / kBN) * ((M + w - 1) / w);
+    const int64_t cost = ((tiles + sms - 1) / sms) * (w + 32);
+    if (cost < best_cost) best = w, best_cost = cost;
+  }
+  return best;
+}
+
 // Tile configuration for M > 64 tokens.  The environment variable MES_GEMM_CONFIG (read
-// once) selects among the compiled variants for tuning: 0 = persistent, 256 tokens,
-// dequantised A in shared memory (default); 1 = persistent, 192 tokens, dequantised A in
-// TMEM (measured ~1.3x slower per MMA for this shape); 2 = one 256-token tile per CTA.
+// once) selects among the compiled variants for tuning: 0 = persistent, token-tile width
+// from persistent_tile_tokens, dequantised A in shared memory (default); 1 = persistent,
+// 192 tokens, dequantised A in TMEM (measured ~1.3x slower per MMA for this shape);
+// 2 = one 256-token tile per CTA; 3 = persistent, always 256 tokens.
 int large_m_config() {
   static int cfg = [] {
     const char* v = getenv("MES_GEMM_CONFIG");
     int c = v ? atoi(v) : 0;
-    return (c < 0 || c > 2) ? 0 : c;
+    return (c < 0 || c > 3) ? 0 : c;
   }();
   return cfg;
 }
@@ -804,7 +824,13 @@ int dispatch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* 
   switch (large_m_config()) {
     case 1: return launch_gemm_persistent<192, 4, 4, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
     case 2: return launch_gemm<256, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-    default: return launch_gemm_persistent<256, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+    case 3: return launch_gemm_persistent<256, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+    default:
+      switch (persistent_tile_tokens(M, N)) {
+        case 192: return launch_gemm_persistent<192, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+        case 224: return launch_gemm_persistent<224, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+        default: return launch_gemm_persistent<256, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+      }
   }
 }
 
