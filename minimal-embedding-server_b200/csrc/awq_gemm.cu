@@ -59,7 +59,9 @@ __device__ __forceinline__ void silu_chunk(const uint32_t (&v)[CHUNK], int lane,
     const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
     const float g = lo ? __uint_as_float(v[j]) : recv;
     const float u = lo ? recv : __uint_as_float(v[H + j]);
-    const float o = g * __frcp_rn(1.0f + __expf(-g)) * u;
+    // silu(g) = g / (1 + e^-g); the approximate divide needs no special-case path, and for
+    // g < -88 (e^-g = inf) it returns 0, the limit of silu.
+    const float o = __fdividef(g, 1.0f + __expf(-g)) * u;
     buf[((lo ? 0 : H) + j) * 16 + f] = __float2bfloat16_rn(o);
   }
   mes::fence_proxy_async_smem();
@@ -518,8 +520,9 @@ awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
         mes::tc_fence_after();
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % SST, a = it % C::kASlots;
-          if (!mes::mbar_wait(&full[s], (it / SST) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT) ||
-              !mes::mbar_wait(&afull[a], (it / C::kASlots) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
+          // afull implies full: every dequant warp waited for the whole stage (X included)
+          // before arriving, so one barrier check per k-step suffices.
+          if (!mes::mbar_wait(&afull[a], (it / C::kASlots) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
             ok = false;
             break;
           }
@@ -678,6 +681,322 @@ awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
   }
 }
 
+// ----------------------------------------------------------------------------------------
+// Pair variant (clusters of two CTAs on neighbouring SMs, tcgen05 cta_group::2).  A pair
+// computes a 256-feature x 256-token tile: CTA r dequantises features [128r, 128r + 128)
+// of the tile and stages tokens [128r, 128r + 128) of X; one MMA of M = 256, N = 256 in
+// the even CTA reads A's rows and B's rows from both CTAs' shared memory and leaves each
+// CTA's 128 features x 256 tokens in that CTA's TMEM.  Against the single-CTA kernel every
+// SM stages and reads half the X bytes per k-step (tensor-core operand reads 32 KB instead
+// of 48 KB, TMA writes 20.5 KB instead of 36.5 KB), which both lowers the shared-memory
+// traffic that bounds the single-CTA mainloop and makes room for a five-deep ring.
+// Roles per CTA are those of the single-CTA kernel; the MMA warp of the odd CTA only takes
+// part in the TMEM allocation.  Barriers:
+//   full_x[s]  (even CTA)  both X halves landed: expect_tx by the even producer, complete_tx
+//                          from both CTAs' loads; waited for by the even CTA's dequant warps,
+//                          so the MMA's wait on afull covers it;
+//   full_w[s]  (each CTA)  the CTA's weight words, scales and zeros landed;
+//   afull[s]   (even CTA)  A rows of both CTAs written: 4 dequant warps of each CTA arrive;
+//   empty[s]   (each CTA)  the stage's MMAs done (commit multicast to both CTAs);
+//   acc_full[b] (each CTA) accumulator b complete (commit multicast);
+//   acc_empty[b] (even CTA) accumulator b drained in both CTAs (8 epilogue warps each).
+template <int EPI>
+struct QCfg {
+  static constexpr bool kResidual = EPI == kEpiResidual, kSilu = EPI == kEpiSilu;
+  // The residual epilogue stages nothing in shared memory, which leaves room for a sixth stage.
+  static constexpr int SST = kResidual ? 6 : 5, SETS = 2;
+  static constexpr int kDqWarps = 4 * SETS;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kThreads = (2 + kDqWarps + kEpiWarps) * 32;
+  static constexpr int kTileN = 2 * kBN;   // features per pair tile
+  static constexpr int kTileT = 256;       // tokens per pair tile
+  static constexpr int kHalfT = kTileT / 2;
+  static constexpr int kXStage = kHalfT * kBK * 2;
+  static constexpr int kAStage = kBN * kBK * 2;
+  static constexpr int kWBytes = (kBK / 8) * kBN * 4;
+  static constexpr int kSBytes = kBN * 2;
+  static constexpr int kZBytes = (kBN / 8) * 4;
+  static constexpr int kWStage = kWBytes + 256 + 128;
+  static constexpr int kChunk = kResidual ? 16 : 32;
+  static constexpr int kOutBuf = kChunk * 32 * 2;
+  static constexpr int kOffX = 0;
+  static constexpr int kOffA = SST * kXStage;
+  static constexpr int kOffW = kOffA + SST * kAStage;
+  static constexpr int kOffOut = kOffW + SST * kWStage;
+  static constexpr int kOffBar = kOffOut + (kResidual ? 0 : kEpiWarps * kOutBuf);
+  static constexpr int kSmem = kOffBar + 512 + 1024;
+  static_assert(kSmem <= 232448, "shared memory budget");
+  static_assert((4 * SST + 4) * 8 + 8 <= 512, "barrier area");
+  static_assert(kSBytes == 256 && kZBytes == 64 && kWStage % 128 == 0, "stage layout");
+  static_assert(kXStage % 1024 == 0 && kAStage % 1024 == 0, "swizzle atoms");
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(QCfg<EPI>::kThreads, 1)
+awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
+                     const __grid_constant__ CUtensorMap map_w,
+                     const __grid_constant__ CUtensorMap map_s,
+                     const __grid_constant__ CUtensorMap map_z,
+                     const __grid_constant__ CUtensorMap map_y,
+                     const __nv_bfloat16* __restrict__ bias, float* __restrict__ R, int64_t ldr,
+                     int M, int N, int K) {
+  using C = QCfg<EPI>;
+  constexpr int SST = C::SST;
+  constexpr uint32_t kTmemCols = 512;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* xs = smem + C::kOffX;
+  uint8_t* as = smem + C::kOffA;
+  uint8_t* wst = smem + C::kOffW;
+  __nv_bfloat16* outbuf = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffOut);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* full_x = bars;              // [SST]
+  uint64_t* full_w = bars + SST;        // [SST]
+  uint64_t* afull = bars + 2 * SST;     // [SST]
+  uint64_t* empty = bars + 3 * SST;     // [SST]
+  uint64_t* acc_full = bars + 4 * SST;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = mes::warp_id(), lane = mes::lane_id();
+  const uint32_t rank = mes::cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int nk = K / kBK;
+  const int num_n = N / C::kTileN;
+  const int num_tiles = num_n * ((M + C::kTileT - 1) / C::kTileT);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SST; ++s) {
+      mes::mbar_init(&full_x[s], 1);
+      mes::mbar_init(&full_w[s], 1);
+      mes::mbar_init(&afull[s], 8);
+      mes::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mes::mbar_init(&acc_full[b], 1);
+      mes::mbar_init(&acc_empty[b], 2 * C::kEpiWarps);
+    }
+    *abort_flag = 0;
+    mes::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    mes::tma_prefetch_desc(&map_x);
+    mes::tma_prefetch_desc(&map_w);
+    mes::tma_prefetch_desc(&map_s);
+    mes::tma_prefetch_desc(&map_z);
+    if (EPI == kEpiBf16) mes::tma_prefetch_desc(&map_y);
+  }
+  if (warp == 1) {
+    __syncwarp();
+    mes::tmem_alloc2(tmem_slot, kTmemCols);
+    mes::tmem_relinquish2();
+  }
+  mes::tc_fence_before();
+  mes::cluster_sync();  // both CTAs' barriers are initialised before either signals the other
+  mes::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------- TMA producer -------------------------------------
+    if (lane == 0) {
+      const uint32_t full_x0 = mes::mapa_shared(mes::smem_u32(full_x), 0);
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        const int n0 = (tile % num_n) * C::kTileN + (int)rank * kBN;
+        const int t0 = (tile / num_n) * C::kTileT + (int)rank * C::kHalfT;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % SST;
+          if (it >= SST &&
+              !mes::mbar_wait(&empty[s], ((it / SST) & 1) ^ 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mes::mbar_arrive_expect_tx(&full_x[s], 2 * C::kXStage);
+          mes::tma_load_2d_pair(xs + s * C::kXStage, &map_x, full_x0 + 8 * s, kb * kBK, t0);
+          uint8_t* w = wst + s * C::kWStage;
+          mes::mbar_arrive_expect_tx(&full_w[s], C::kWBytes + C::kSBytes + C::kZBytes);
+          mes::tma_load_2d(w, &map_w, &full_w[s], n0, kb * (kBK / 8));
+          mes::tma_load_2d(w + C::kWBytes, &map_s, &full_w[s], n0, kb / 2);
+          mes::tma_load_2d(w + C::kWBytes + 256, &map_z, &full_w[s], n0 / 8, kb / 2);
+        }
+      }
+      if (!ok) {
+        const uint64_t t = mes::globaltimer_ns();  // let issued copies land
+        while (mes::globaltimer_ns() - t < 1000000ull) {
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------- MMA issuer (even CTA) ----------------------------
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = mes::idesc_bf16_f32(2 * kBN, C::kTileT, false);
+      const uint32_t xs_addr = mes::smem_u32(xs), as_addr = mes::smem_u32(as);
+      int it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++lt) {
+        const int b = lt & 1;
+        if (lt >= 2 &&
+            !mes::mbar_wait(&acc_empty[b], ((lt >> 1) - 1) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
+          ok = false;
+          break;
+        }
+        mes::tc_fence_after();
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % SST;
+          // afull implies full_x: the even CTA's dequant warps wait for both X halves before
+          // arriving, so one barrier check per k-step suffices.
+          if (!mes::mbar_wait(&afull[s], (it / SST) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          mes::tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t adesc = mes::smem_desc_sw128(as_addr + s * C::kAStage + kk * 32, 16, 1024);
+            const uint64_t bdesc = mes::smem_desc_sw128(xs_addr + s * C::kXStage + kk * 32, 16, 1024);
+            mes::mma_ss2(tmem + b * C::kTileT, adesc, bdesc, idesc, (kb | kk) != 0);
+          }
+          mes::tc_commit2_mc(&empty[s], 0x3);
+        }
+        if (ok) mes::tc_commit2_mc(&acc_full[b], 0x3);
+      }
+      if (!ok) {
+        const uint64_t t = mes::globaltimer_ns();  // let issued MMAs finish
+        while (mes::globaltimer_ns() - t < 1000000ull) {
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp < 2 + C::kDqWarps) {
+    // --------------------------------- dequant ----------------------------------------
+    const int set = (warp - 2) / 4;
+    const int row = (warp & 3) * 32 + lane;
+    const int zshift = 4 * kInvOrder[row & 7];  // n0 is a multiple of 128
+    const uint32_t afull0 = mes::mapa_shared(mes::smem_u32(afull), 0);
+    int it = 0;
+    bool ok = true;
+    for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        if (it % C::SETS != set) continue;
+        const int s = it % SST;
+        // The A slot of a stage is free once the stage's weights landed again: the producer
+        // refills a stage only after its MMAs completed.
+        if (!mes::mbar_wait_warp(&full_w[s], (it / SST) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT) ||
+            (rank == 0 &&
+             !mes::mbar_wait_warp(&full_x[s], (it / SST) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT))) {
+          ok = false;
+          break;
+        }
+        const uint8_t* w = wst + s * C::kWStage;
+        const GroupParams gp =
+            make_group(reinterpret_cast<const uint32_t*>(w + C::kWBytes + 256)[row >> 3], zshift,
+                       reinterpret_cast<const uint16_t*>(w + C::kWBytes)[row]);
+        const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(w) + row;
+        uint32_t av[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t v = wsrc[i * kBN];
+          av[4 * i + 0] = dq_pair(v, gp);
+          av[4 * i + 1] = dq_pair(v >> 4, gp);
+          av[4 * i + 2] = dq_pair(v >> 8, gp);
+          av[4 * i + 3] = dq_pair(v >> 12, gp);
+        }
+        // Row `row` of the 128 x 64 K-major tile, 128-byte swizzle: 16-byte chunk i
+        // (k = 8i .. 8i+7) lives at chunk position i ^ (row & 7).
+        uint8_t* arow = as + s * C::kAStage + row * 128;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          *reinterpret_cast<uint4*>(arow + ((i ^ (row & 7)) * 16)) =
+              make_uint4(av[4 * i], av[4 * i + 1], av[4 * i + 2], av[4 * i + 3]);
+        mes::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mes::mbar_arrive_remote(afull0 + 8 * s);
+        __syncwarp();
+      }
+    }
+  } else {
+    // --------------------------------- epilogue ---------------------------------------
+    const int q = warp & 3;
+    const int eh = (warp - 2 - C::kDqWarps) / 4;  // which alternate chunks this warp drains
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t acc_empty0 = mes::mapa_shared(mes::smem_u32(acc_empty), 0);
+    __nv_bfloat16* buf = outbuf + (warp - 2 - C::kDqWarps) * (C::kOutBuf / 2);
+    bool stored = false;
+    int lt = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++lt) {
+      const int b = lt & 1;
+      const int n0 = (tile % num_n) * C::kTileN + (int)rank * kBN;
+      const int t0 = (tile / num_n) * C::kTileT;
+      const int n = n0 + q * 32 + lane;
+      if (!mes::mbar_wait_warp(&acc_full[b], (lt >> 1) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT))
+        break;
+      mes::tc_fence_after();
+      const float bv = bias ? __bfloat162float(bias[n]) : 0.f;
+#pragma unroll 1
+      for (int c0 = eh * C::kChunk; c0 < C::kTileT; c0 += 2 * C::kChunk) {
+        uint32_t v[C::kChunk];
+        if constexpr (C::kChunk == 32) mes::tmem_ld32(tmem + lane_off + b * C::kTileT + c0, v);
+        else mes::tmem_ld16(tmem + lane_off + b * C::kTileT + c0, v);
+        mes::tmem_wait_ld();
+        if (t0 + c0 >= M) continue;  // rows past the end of X
+        if constexpr (C::kSilu) {
+          silu_chunk<C::kChunk>(v, lane, buf, stored, &map_y, n0 / 2 + q * 16, t0 + c0);
+        } else if constexpr (C::kResidual) {
+          const int rows = min(C::kChunk, M - (t0 + c0));
+          float* rp = R + (int64_t)(t0 + c0) * ldr + n;
+          float rv[C::kChunk];
+#pragma unroll
+          for (int j = 0; j < C::kChunk; ++j) rv[j] = j < rows ? rp[(int64_t)j * ldr] : 0.f;
+#pragma unroll
+          for (int j = 0; j < C::kChunk; ++j)
+            if (j < rows) rp[(int64_t)j * ldr] = rv[j] + (__uint_as_float(v[j]) + bv);
+        } else {
+          if (stored) {
+            if (lane == 0) mes::tma_store_wait_read<0>();
+            __syncwarp();
+          }
+#pragma unroll
+          for (int j = 0; j < C::kChunk; j += 2) {  // one bf16x2 conversion per two values
+            const uint32_t pk = mes::pack_bf16x2(__uint_as_float(v[j]) + bv, __uint_as_float(v[j + 1]) + bv);
+            buf[j * 32 + lane] = __ushort_as_bfloat16(static_cast<unsigned short>(pk & 0xFFFFu));
+            buf[(j + 1) * 32 + lane] = __ushort_as_bfloat16(static_cast<unsigned short>(pk >> 16));
+          }
+          mes::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mes::tma_store_2d(&map_y, buf, n0 + q * 32, t0 + c0);
+            mes::tma_store_commit();
+          }
+          __syncwarp();
+          stored = true;
+        }
+      }
+      // The accumulator is free once every tcgen05.ld above has completed, in both CTAs.
+      mes::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mes::mbar_arrive_remote(acc_empty0 + 8 * b);
+      __syncwarp();
+    }
+    if (!C::kResidual) {
+      if (lane == 0) mes::tma_store_wait_all<0>();
+      __syncwarp();
+    }
+  }
+
+  mes::tc_fence_before();
+  __syncthreads();
+  mes::cluster_sync();  // no signal of either CTA can reach a CTA that has left
+  if (warp == 1) {
+    __syncwarp();
+    mes::tc_fence_after();
+    mes::tmem_dealloc2(tmem, kTmemCols);
+  }
+}
+
 // ------------------------------------ repack ----------------------------------------------
 // out[b, n] = sum_i code(k = 8b + order[i], n) << 4i, order = {0,2,4,6,1,3,5,7}.
 __global__ void awq_repack_kernel(const uint32_t* __restrict__ in, int64_t K, int64_t N,
@@ -781,35 +1100,69 @@ int launch_gemm_persistent(const void* X, int64_t ldx, const int32_t* qw, const 
   return mes_host::from_cuda(cudaGetLastError());
 }
 
-// Token-tile width of the persistent kernel for an M x N product.  Every CTA walks
-// ceil(tiles / SMs) tiles at most, so the launch takes about that many tile times; a tile's
-// time grows with its width plus a fixed per-tile cost (the pipeline fill and the
-// accumulator hand-over), worth about 32 tokens.  The width that minimises
-// waves x (width + 32) is taken, the wider one on ties; e.g. N = 1024, M = 20000 on 148
-// SMs: 256 -> 632 tiles, 5 waves; 224 -> 720 tiles, 5 waves of shorter tiles.
-int persistent_tile_tokens(int64_t M, int64_t N) {
-  const int64_t sms = mes_host::sm_count();
-  const int widths[3] = {256, 224, 192};
-  int best = 256;
-  int64_t best_cost = INT64_MAX;
-  for (int w : widths) {
-    const int64_t tiles = (N / kBN) * ((M + w - 1) / w);
-    const int64_t cost = ((tiles + sms - 1) / sms) * (w + 32);
-    if (cost < best_cost) best = w, best_cost = cost;
-  }
-  return best;
+// Pair kernel launch: clusters of two CTAs, as many pairs as can be resident at once
+// (at most one per two SMs) and no more than there are pair tiles.
+template <int EPI>
+int launch_gemm_pair(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
+                     const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
+                     int64_t N, int64_t K, cudaStream_t stream) {
+  using C = QCfg<EPI>;
+  auto kern = awq_gemm_pair_kernel<EPI>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  if (e != cudaSuccess) return MES_ERR_CUDA;
+  CUtensorMap mx, mw, ms, mz, my;
+  if (!mes_host::make_map_2d(&mx, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, ldx, C::kHalfT,
+                             kBK, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !mes_host::make_map_2d(&mw, qw, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, K / 8, N, N, kBK / 8, kBN,
+                             CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !mes_host::make_map_2d(&ms, scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, K / kGroup, N, N, 1,
+                             kBN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !mes_host::make_map_2d(&mz, qzeros, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, K / kGroup, N / 8,
+                             N / 8, 1, kBN / 8, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return MES_ERR_INVALID;
+  if (!make_out_map(&my, mx, EPI, Y, M, N, ldy, C::kChunk)) return MES_ERR_INVALID;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(C::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(2, 1, 1);
+  int clusters = 0;
+  e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+  if (e != cudaSuccess || clusters < 1) return MES_ERR_CUDA;
+  const int64_t tiles = (N / C::kTileN) * ((M + C::kTileT - 1) / C::kTileT);
+  const int64_t pairs = tiles < clusters ? tiles : clusters;
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, mx, mw, ms, mz, my, (const __nv_bfloat16*)bias,
+                         C::kResidual || C::kSilu ? (float*)Y : nullptr, ldy, (int)M, (int)N, (int)K);
+  if (e != cudaSuccess) return MES_ERR_CUDA;
+  return mes_host::from_cuda(cudaGetLastError());
 }
 
 // Tile configuration for M > 64 tokens.  The environment variable MES_GEMM_CONFIG (read
-// once) selects among the compiled variants for tuning: 0 = persistent, token-tile width
-// from persistent_tile_tokens, dequantised A in shared memory (default); 1 = persistent,
-// 192 tokens, dequantised A in TMEM (measured ~1.3x slower per MMA for this shape);
-// 2 = one 256-token tile per CTA; 3 = persistent, always 256 tokens.
+// once) selects among the compiled variants for tuning:
+//   0 (default) the residual epilogue on CTA pairs where N is a multiple of 256, the other
+//     epilogues on single CTAs (measured at M = 20000: residual N = 1024, K = 2048 865 vs
+//     788 TFLOP/s; bf16 N = 6144, K = 1024 1138 vs 1170; SiLU 1117 vs 1159);
+//   1 persistent single CTA, 192 tokens, dequantised A in TMEM;
+//   2 one 256-token tile per CTA;
+//   3 persistent single CTA, 256 tokens, dequantised A in shared memory;
+//   4 CTA pairs wherever N is a multiple of 256.
+// Narrower single-CTA tiles do not pay: a tile's time is set by its 128 x K weights far
+// more than by its token count (measured 1087 / 871 / 622 TFLOP/s for 256 / 192 / 128
+// tokens at M = 20000, N = 6144, K = 1024), so the widest tile wins even where a narrower
+// one would fill the last wave better.
 int large_m_config() {
   static int cfg = [] {
     const char* v = getenv("MES_GEMM_CONFIG");
     int c = v ? atoi(v) : 0;
-    return (c < 0 || c > 3) ? 0 : c;
+    return (c < 0 || c > 4) ? 0 : c;
   }();
   return cfg;
 }
@@ -825,12 +1178,13 @@ int dispatch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* 
     case 1: return launch_gemm_persistent<192, 4, 4, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
     case 2: return launch_gemm<256, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
     case 3: return launch_gemm_persistent<256, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+    case 4:
+      if (N % (2 * kBN) == 0) return launch_gemm_pair<EPI>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+      return launch_gemm_persistent<256, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
     default:
-      switch (persistent_tile_tokens(M, N)) {
-        case 192: return launch_gemm_persistent<192, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-        case 224: return launch_gemm_persistent<224, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-        default: return launch_gemm_persistent<256, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-      }
+      if (EPI == kEpiResidual && N % (2 * kBN) == 0)
+        return launch_gemm_pair<EPI>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+      return launch_gemm_persistent<256, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
   }
 }
 

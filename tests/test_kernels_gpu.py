@@ -270,8 +270,7 @@ sys.path.insert(0, sys.argv[1])
 import __graft_entry__; __graft_entry__.load_package()
 from mes_b200 import _C
 from oracle import awq as oawq
-# (20000, 256, 1024) spans several waves of the GPU, so the default configuration picks a
-# different token-tile width for it than for the single-wave shapes.
+# (20000, 256, 1024) spans several waves of the persistent kernel's CTAs.
 for M, K, N, res in [(16, 256, 256, False), (65, 256, 128, False), (300, 1024, 384, True), (777, 3072, 1024, False), (1000, 1024, 256, True), (20000, 256, 1024, True)]:
     qw, qz, sc = oawq.random_awq(K, N, seed=M)
     g = torch.Generator().manual_seed(M)
@@ -306,7 +305,7 @@ print("ok")
 """
 
 
-@pytest.mark.parametrize("config", ["0", "1", "2", "3"])
+@pytest.mark.parametrize("config", ["0", "1", "2", "3", "4"])
 def test_awq_gemm_tile_variants(config):
     # The large-M tile variant is chosen once per process (MES_GEMM_CONFIG), so each runs
     # in a child process; same tolerances as test_awq_gemm_matches_fp32 and the residual
