@@ -44,6 +44,12 @@ const char* mes_status_string(int status);
  * library on the current device (0 if none).  Synchronises the current device. */
 int mes_take_device_error(int* code);
 
+/* Leaves `sms` SMs (0..64) free of the persistent kernels (AWQ GEMM, attention) so that
+ * another kernel running concurrently - an NCCL all-reduce overlapped on its own stream -
+ * delays none of their CTAs.  Process-wide; 0 (the default) uses every SM.  No counterpart
+ * in the reference, whose collectives do not overlap its GEMMs. */
+int mes_set_sm_reserve(int sms);
+
 /* ---------------------------------------------------------------------------------
  * Embedding gather.  out[t, :] = table[ids[t], :].
  * Replaces VocabParallelEmbedding.forward (layers/embed_head.py:43-52); the table is

@@ -22,6 +22,7 @@ SIGNATURES = {
     "mes_version": (_i32, []),
     "mes_status_string": (ctypes.c_char_p, [_i32]),
     "mes_take_device_error": (_i32, [ctypes.POINTER(_i32)]),
+    "mes_set_sm_reserve": (_i32, [_i32]),
     "mes_embedding": (_i32, [_vp, _i64, _vp, _i64, _i64, _vp, _vp]),
     "mes_embedding_f32": (_i32, [_vp, _i64, _vp, _i64, _i64, _vp, _vp]),
     "mes_rmsnorm": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _vp]),
@@ -58,6 +59,14 @@ launch_count = 0
 # awq_gemm_residual call appends (start_event, end_event, flops, (kind, M, N, K)) recorded
 # on the launching stream.
 gemm_events = None
+# Epilogue kinds ("bf16", "residual", "silu") whose GEMMs append to gemm_events; None = all.
+gemm_event_kinds = None
+
+
+def _timing_event():
+    # external: inside a CUDA-graph capture the record becomes a graph node, so the events
+    # time the kernel on every replay
+    return torch.cuda.Event(enable_timing=True, external=True)
 
 
 class MesError(RuntimeError):
@@ -91,13 +100,16 @@ def _check(code: int, what: str, launches: int = 1) -> None:
 
 
 def _p(t):
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    return None if t is None else t.data_ptr()   # c_void_p arguments take plain ints
+
+
+_raw_stream = torch._C._cuda_getCurrentRawStream
 
 
 def _stream(t: torch.Tensor):
     if not t.is_cuda:
         raise MesError("mes_b200 kernels need CUDA tensors (there is no CPU path)")
-    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+    return _raw_stream(t.device.index)
 
 
 def _need(cond: bool, msg: str) -> None:
@@ -109,6 +121,11 @@ def take_device_error() -> int:
     code = _i32(0)
     _check(lib().mes_take_device_error(ctypes.byref(code)), "mes_take_device_error", 0)
     return code.value
+
+
+def set_sm_reserve(sms: int) -> None:
+    """Keep ``sms`` SMs free of the persistent kernels (see ``mes_set_sm_reserve``)."""
+    _check(lib().mes_set_sm_reserve(int(sms)), "mes_set_sm_reserve", 0)
 
 
 # --------------------------------------------------------------------------------------
@@ -290,9 +307,9 @@ def awq_gemm_residual(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.
     K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
     M = x.shape[0]
     _need(x.shape[1] == K and tuple(residual.shape) == (M, N), "shape mismatch")
-    ev = gemm_events
+    ev = gemm_events if gemm_event_kinds is None or "residual" in gemm_event_kinds else None
     if ev is not None:
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, e1 = _timing_event(), _timing_event()
         e0.record()
     _check(lib().mes_awq_gemm_residual(_p(x), x.stride(0), _p(qweight_mes), _p(qzeros),
                                        _p(scales), _p(bias), _p(residual), residual.stride(0),
@@ -315,9 +332,9 @@ def awq_gemm_silu(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tens
     _need(x.shape[1] == K, f"x has K={x.shape[1]}, weight has K={K}")
     if out is None:
         out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=x.device)
-    ev = gemm_events
+    ev = gemm_events if gemm_event_kinds is None or "silu" in gemm_event_kinds else None
     if ev is not None:
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, e1 = _timing_event(), _timing_event()
         e0.record()
     _check(lib().mes_awq_gemm_silu(_p(x), x.stride(0), _p(qweight_mes), _p(qzeros), _p(scales),
                                    _p(out), out.stride(0), M, N, K, group_size, _stream(x)),
@@ -353,9 +370,9 @@ def awq_gemm(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
     _need(x.shape[1] == K, f"x has K={x.shape[1]}, weight has K={K}")
     if out is None:
         out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
-    ev = gemm_events
+    ev = gemm_events if gemm_event_kinds is None or "bf16" in gemm_event_kinds else None
     if ev is not None:
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, e1 = _timing_event(), _timing_event()
         e0.record()
     _check(lib().mes_awq_gemm(_p(x), x.stride(0), _p(qweight_mes), _p(qzeros), _p(scales),
                               _p(bias), _p(out), out.stride(0), M, N, K, group_size,

@@ -762,9 +762,15 @@ static int poly_pairs() {
 // the CTA at launch: three warps per sub-partition, one of them shrinking.
 template <typename K>
 static bool pair_kernel_registers_fit(K kern) {
-  cudaFuncAttributes a;
-  if (cudaFuncGetAttributes(&a, kern) != cudaSuccess) return false;
-  return 3 * a.numRegs >= 2 * kSoftmaxRegs + kOtherRegs && a.maxThreadsPerBlock >= kPThreads;
+  static std::atomic<int> fit{-1};  // the compiled register count is the same on every device
+  int f = fit.load(std::memory_order_relaxed);
+  if (f < 0) {
+    cudaFuncAttributes a;
+    if (cudaFuncGetAttributes(&a, kern) != cudaSuccess) return false;
+    f = 3 * a.numRegs >= 2 * kSoftmaxRegs + kOtherRegs && a.maxThreadsPerBlock >= kPThreads;
+    fit.store(f, std::memory_order_relaxed);
+  }
+  return f != 0;
 }
 
 // Workspace layout is defined next to mes_varlen_schedule (elementwise.cu).
@@ -784,7 +790,7 @@ extern "C" int mes_varlen_attention(const void* qkv, int64_t ld, void* out, cons
     return MES_ERR_INVALID;
   const char* ws = static_cast<const char*>(workspace);
   const int64_t items_off = ((256 + 4 * (T + 1)) + 255) & ~int64_t(255);
-  const int grid = mes_host::sm_count();
+  const int grid = mes_host::persistent_ctas();
   const float scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t s = (cudaStream_t)stream;
   const int poly = poly_pairs();
@@ -793,16 +799,23 @@ extern "C" int mes_varlen_attention(const void* qkv, int64_t ld, void* out, cons
               : poly == 4 ? varlen_attention_pair_kernel<4>
                           : varlen_attention_pair_kernel<0>;
   if ((Hq / Hkv) % 2 == 0 && pair_kernel_registers_fit(kern)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
-    if (e != cudaSuccess) return MES_ERR_CUDA;
+    static std::atomic<uint64_t> attr_done[4];
+    const int st = mes_host::once_per_device(attr_done[poly == 2 ? 1 : poly == 3 ? 2 : poly == 4 ? 3 : 0], [&] {
+      return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem) == cudaSuccess
+                 ? MES_OK : MES_ERR_CUDA;
+    });
+    if (st != MES_OK) return st;
     kern<<<grid, kPThreads, kPSmem, s>>>(map, (__nv_bfloat16*)out, (const int*)ws,
                                          (const int*)(ws + 256), (const int2*)(ws + items_off),
                                          Hq, Hkv, scale_log2);
     return mes_host::from_cuda(cudaGetLastError());
   }
-  cudaError_t e = cudaFuncSetAttribute(varlen_attention_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-  if (e != cudaSuccess) return MES_ERR_CUDA;
+  static std::atomic<uint64_t> attr_done1{0};
+  const int st = mes_host::once_per_device(attr_done1, [] {
+    return cudaFuncSetAttribute(varlen_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kSmem) == cudaSuccess ? MES_OK : MES_ERR_CUDA;
+  });
+  if (st != MES_OK) return st;
   varlen_attention_kernel<<<grid, kThreads, kSmem, s>>>(
       map, (__nv_bfloat16*)out, (const int*)ws, (const int*)(ws + 256), (const int2*)(ws + items_off),
       Hq, Hkv, scale_log2);

@@ -1056,9 +1056,13 @@ int launch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qz
                 const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
                 int64_t N, int64_t K, cudaStream_t stream) {
   using C = Cfg<BT, STAGES, EPI, NDQ>;
-  cudaError_t e = cudaFuncSetAttribute(awq_gemm_kernel<BT, STAGES, EPI, NDQ>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-  if (e != cudaSuccess) return MES_ERR_CUDA;
+  static std::atomic<uint64_t> attr_done{0};
+  const int st = mes_host::once_per_device(attr_done, [] {
+    return cudaFuncSetAttribute(awq_gemm_kernel<BT, STAGES, EPI, NDQ>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) == cudaSuccess
+               ? MES_OK : MES_ERR_CUDA;
+  });
+  if (st != MES_OK) return st;
   CUtensorMap mx, mw, my;
   if (!mes_host::make_map_2d(&mx, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, ldx, BT, kBK,
                              CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1078,9 +1082,13 @@ int launch_gemm_persistent(const void* X, int64_t ldx, const int32_t* qw, const 
                            const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
                            int64_t N, int64_t K, cudaStream_t stream) {
   using C = PCfg<BT, SST, AST, EPI, SETS>;
-  cudaError_t e = cudaFuncSetAttribute(awq_gemm_persistent_kernel<BT, SST, AST, EPI, SETS>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-  if (e != cudaSuccess) return MES_ERR_CUDA;
+  static std::atomic<uint64_t> attr_done{0};
+  const int st = mes_host::once_per_device(attr_done, [] {
+    return cudaFuncSetAttribute(awq_gemm_persistent_kernel<BT, SST, AST, EPI, SETS>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) == cudaSuccess
+               ? MES_OK : MES_ERR_CUDA;
+  });
+  if (st != MES_OK) return st;
   CUtensorMap mx, mw, ms, mz, my;
   if (!mes_host::make_map_2d(&mx, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, ldx, BT, kBK,
                              CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1093,7 +1101,8 @@ int launch_gemm_persistent(const void* X, int64_t ldx, const int32_t* qw, const 
     return MES_ERR_INVALID;
   if (!make_out_map(&my, mx, EPI, Y, M, N, ldy, C::kChunk)) return MES_ERR_INVALID;
   const int64_t tiles = (N / kBN) * ((M + BT - 1) / BT);
-  const int grid = (int)(tiles < mes_host::sm_count() ? tiles : mes_host::sm_count());
+  const int ctas = mes_host::persistent_ctas();
+  const int grid = (int)(tiles < ctas ? tiles : ctas);
   awq_gemm_persistent_kernel<BT, SST, AST, EPI, SETS><<<grid, C::kThreads, C::kSmem, stream>>>(
       mx, mw, ms, mz, my, (const __nv_bfloat16*)bias, C::kResidual ? (float*)Y : nullptr, ldy,
       (int)M, (int)N, (int)K);
@@ -1108,8 +1117,12 @@ int launch_gemm_pair(const void* X, int64_t ldx, const int32_t* qw, const int32_
                      int64_t N, int64_t K, cudaStream_t stream) {
   using C = QCfg<EPI>;
   auto kern = awq_gemm_pair_kernel<EPI>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-  if (e != cudaSuccess) return MES_ERR_CUDA;
+  static std::atomic<uint64_t> attr_done{0};
+  const int st = mes_host::once_per_device(attr_done, [&] {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) == cudaSuccess
+               ? MES_OK : MES_ERR_CUDA;
+  });
+  if (st != MES_OK) return st;
   CUtensorMap mx, mw, ms, mz, my;
   if (!mes_host::make_map_2d(&mx, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, ldx, C::kHalfT,
                              kBK, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1133,13 +1146,21 @@ int launch_gemm_pair(const void* X, int64_t ldx, const int32_t* qw, const int32_
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cfg.gridDim = dim3(2, 1, 1);
-  int clusters = 0;
-  e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
-  if (e != cudaSuccess || clusters < 1) return MES_ERR_CUDA;
+  // Resident pairs, queried once per device.
+  static std::atomic<int> clusters_by_dev[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MES_ERR_CUDA;
+  int clusters = clusters_by_dev[dev & 63].load(std::memory_order_relaxed);
+  if (clusters <= 0) {
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
+      return MES_ERR_CUDA;
+    clusters_by_dev[dev & 63].store(clusters, std::memory_order_relaxed);
+  }
   const int64_t tiles = (N / C::kTileN) * ((M + C::kTileT - 1) / C::kTileT);
-  const int64_t pairs = tiles < clusters ? tiles : clusters;
+  const int64_t max_pairs = clusters < mes_host::persistent_ctas() / 2 ? clusters : mes_host::persistent_ctas() / 2;
+  const int64_t pairs = tiles < max_pairs ? tiles : max_pairs;
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
-  e = cudaLaunchKernelEx(&cfg, kern, mx, mw, ms, mz, my, (const __nv_bfloat16*)bias,
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mx, mw, ms, mz, my, (const __nv_bfloat16*)bias,
                          C::kResidual || C::kSilu ? (float*)Y : nullptr, ldy, (int)M, (int)N, (int)K);
   if (e != cudaSuccess) return MES_ERR_CUDA;
   return mes_host::from_cuda(cudaGetLastError());

@@ -3,6 +3,7 @@
 // wrappers written as inline PTX, and the host-side tensor-map encoder.
 #pragma once
 
+#include <atomic>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -365,5 +366,21 @@ bool make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
 inline int from_cuda(cudaError_t e) { return e == cudaSuccess ? MES_OK : MES_ERR_CUDA; }
 
 int sm_count();
+
+// Runs `fn` (returning a status) once per device for the call site owning `done`: for
+// per-kernel settings such as cudaFuncSetAttribute, which persist in the context, so that
+// launches do not repeat them.  Concurrent first calls may both run `fn`; that is harmless.
+template <typename F>
+int once_per_device(std::atomic<uint64_t>& done, F fn) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MES_ERR_CUDA;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return MES_OK;
+  const int st = fn();
+  if (st == MES_OK) done.fetch_or(bit, std::memory_order_acq_rel);
+  return st;
+}
+// CTAs of a persistent kernel: the SM count less the SMs reserved by mes_set_sm_reserve.
+int persistent_ctas();
 
 }  // namespace mes_host

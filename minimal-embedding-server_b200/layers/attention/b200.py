@@ -24,19 +24,21 @@ _state = threading.local()
 @contextlib.contextmanager
 def batch_schedule(positions: torch.Tensor):
     """Schedule one packed batch on the device and share it with every attention layer
-    called inside the ``with`` block."""
-    prev = getattr(_state, "current", None)
-    _state.current = (positions, _C.varlen_schedule(positions))
+    called inside the ``with`` block for this ``positions`` tensor.  Contexts nest, so the
+    micro-batches of one forward can each hold their own schedule."""
+    prev = getattr(_state, "current", ())
+    entry = (positions, _C.varlen_schedule(positions))
+    _state.current = prev + (entry,)
     try:
-        yield _state.current[1]
+        yield entry[1]
     finally:
         _state.current = prev
 
 
 def _workspace_for(positions: torch.Tensor) -> torch.Tensor:
-    cur = getattr(_state, "current", None)
-    if cur is not None and cur[0] is positions:
-        return cur[1]
+    for pos, ws in reversed(getattr(_state, "current", ())):
+        if pos is positions:
+            return ws
     return _C.varlen_schedule(positions)
 
 

@@ -273,6 +273,11 @@ class RowParallelLinear(LinearBase):
             dist.all_reduce(y)
         return y
 
+    def forward_partial(self, x: torch.Tensor) -> torch.Tensor:
+        """This rank's partial product (bias on rank 0), before the all-reduce - for callers
+        that overlap the reduction with other work."""
+        return self._mm(x, self.bias if self.tp_rank == 0 else None)
+
     def forward_residual(self, x: torch.Tensor, residual: torch.Tensor) -> torch.Tensor | None:
         """Add this projection to the fp32 residual stream.  At tp == 1 the add happens in
         the GEMM epilogue (returns None); at tp > 1 the bf16 partial products are summed

@@ -16,10 +16,13 @@ the projection was already added.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 from torch import nn
 
+from .. import _C
 from ..layers.activation import SiluAndMul
 from ..layers.attention import batch_schedule, create_attention
 from ..layers.embed_head import VocabParallelEmbedding
@@ -95,6 +98,10 @@ class Qwen2Attention(nn.Module):
         """Attention block added into the fp32 residual stream (see module docstring)."""
         return self.o_proj.forward_residual(self._attend(positions, hidden_states), residual)
 
+    def forward_partial(self, positions, hidden_states):
+        """This rank's o_proj partial product, before the all-reduce."""
+        return self.o_proj.forward_partial(self._attend(positions, hidden_states))
+
 
 class Qwen2MLP(nn.Module):
 
@@ -113,12 +120,17 @@ class Qwen2MLP(nn.Module):
     def forward(self, x):
         return self.down_proj(self.act_fn(self.gate_up_proj(x)))
 
-    def forward_residual(self, x, residual):
+    def _act(self, x):
         if self.gate_up_proj.supports_silu():
-            act = self.gate_up_proj.forward_silu(x)   # GEMM with SiLU-and-mul epilogue
-        else:
-            act = self.act_fn(self.gate_up_proj(x))
-        return self.down_proj.forward_residual(act, residual)
+            return self.gate_up_proj.forward_silu(x)   # GEMM with SiLU-and-mul epilogue
+        return self.act_fn(self.gate_up_proj(x))
+
+    def forward_residual(self, x, residual):
+        return self.down_proj.forward_residual(self._act(x), residual)
+
+    def forward_partial(self, x):
+        """This rank's down_proj partial product, before the all-reduce."""
+        return self.down_proj.forward_partial(self._act(x))
 
 
 def _attn_kwargs(model_config, qkv_bias: bool, qk_norm: bool) -> dict:
@@ -186,13 +198,96 @@ class DecoderModel(nn.Module):
                                      for _ in range(mc.num_hidden_layers)])
         self.norm = RMSNorm(mc.hidden_size, eps=mc.rms_norm_eps)
 
-    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+    # Tensor parallelism: below this many tokens the batch is not split for overlap.
+    overlap_min_tokens = int(os.environ.get("MES_TP_OVERLAP_MIN_TOKENS", "4096"))
+    # SMs kept free of the persistent kernels while all-reduces overlap them (the NCCL
+    # kernels' share; bench and server cap NCCL at as many channels).
+    overlap_reserved_sms = int(os.environ.get("MES_TP_RESERVED_SMS", "16"))
+
+    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor,
+                overlap_split: int | None = None) -> torch.Tensor:
+        """``overlap_split``: at tp > 1, the micro-batch boundary (a sequence start) when the
+        caller knows it from the host copy of the batch (see :meth:`overlap_split_host`);
+        otherwise it is derived from ``positions`` with one device synchronisation."""
+        split = overlap_split if _tp_size() > 1 else None
+        if split is None:
+            split = self._overlap_split(positions)
+        if split is not None:
+            return self._forward_overlapped(input_ids, positions, split)
         with batch_schedule(positions):
             hidden_states = self.embed_tokens.forward_f32(input_ids)
             residual = None
             for layer in self.layers:
                 hidden_states, residual = layer(positions, hidden_states, residual)
             return self.norm.residual_norm(residual, hidden_states)
+
+    def _overlap_split(self, positions: torch.Tensor) -> int | None:
+        """Token index of the sequence start nearest the middle of the batch, or None when
+        the forward runs unsplit (tp == 1, a small batch, or a single sequence)."""
+        T = positions.shape[0]
+        if _tp_size() == 1 or T < self.overlap_min_tokens:
+            return None
+        starts = (torch.nonzero(positions[1:] != positions[:-1] + 1).flatten() + 1).cpu()
+        return self._nearest_middle(starts.numpy(), T)
+
+    @classmethod
+    def overlap_split_host(cls, positions) -> int | None:
+        """:meth:`_overlap_split` from a host (numpy) copy of ``positions``."""
+        import numpy as np
+        pos = np.asarray(positions)
+        T = pos.shape[0]
+        if _tp_size() == 1 or T < cls.overlap_min_tokens:
+            return None
+        return cls._nearest_middle(np.flatnonzero(pos[1:] != pos[:-1] + 1) + 1, T)
+
+    @staticmethod
+    def _nearest_middle(starts, T: int) -> int | None:
+        if len(starts) == 0:
+            return None
+        import numpy as np
+        return int(starts[np.argmin(np.abs(np.asarray(starts) - T // 2))])
+
+    def _forward_overlapped(self, input_ids, positions, split: int) -> torch.Tensor:
+        """Tensor-parallel forward as two micro-batches of whole sequences, A = tokens
+        [0, split) and B = [split, T), interleaved per half-block on the compute stream:
+        A's attention, B's attention, A's MLP, B's MLP, ...  Each half-block ends in an
+        asynchronous all-reduce of its partial product, which runs while the other
+        micro-batch computes; the next half-block of the same micro-batch waits for it on
+        the stream (no host synchronisation).  Per token the arithmetic is the unsplit
+        forward's."""
+        T = positions.shape[0]
+        parts = ((0, split), (split, T))
+        pos = [positions[a:b] for a, b in parts]
+        _C.set_sm_reserve(self.overlap_reserved_sms)
+        try:
+            with batch_schedule(pos[0]), batch_schedule(pos[1]):
+                residual = self.embed_tokens.forward_f32(input_ids)
+                res = [residual[a:b] for a, b in parts]
+                pending = [None, None]
+
+                def norm_after(norm, m, out=None):
+                    if pending[m] is None:
+                        return norm.residual_norm(res[m], None, out)
+                    delta, work = pending[m]
+                    work.wait()
+                    return norm.residual_norm(res[m], delta, out)
+
+                for layer in self.layers:
+                    for m in (0, 1):
+                        x = norm_after(layer.input_layernorm, m)
+                        y = layer.self_attn.forward_partial(pos[m], x)
+                        pending[m] = (y, dist.all_reduce(y, async_op=True))
+                    for m in (0, 1):
+                        x = norm_after(layer.post_attention_layernorm, m)
+                        y = layer.mlp.forward_partial(x)
+                        pending[m] = (y, dist.all_reduce(y, async_op=True))
+                out = torch.empty(T, residual.shape[1], dtype=torch.bfloat16,
+                                  device=residual.device)
+                for m, (a, b) in enumerate(parts):
+                    norm_after(self.norm, m, out[a:b])
+                return out
+        finally:
+            _C.set_sm_reserve(0)
 
 
 class Qwen2Model(DecoderModel):
@@ -222,8 +317,9 @@ class CausalLMBase(nn.Module):
             if hasattr(m, "qweight") and hasattr(m, "process_weights_after_loading") and m is not self:
                 m.process_weights_after_loading()
 
-    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
-        return self.model(input_ids, positions)
+    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor,
+                overlap_split: int | None = None) -> torch.Tensor:
+        return self.model(input_ids, positions, overlap_split)
 
 
 @register_model("Qwen2ForCausalLM")

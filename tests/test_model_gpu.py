@@ -68,3 +68,21 @@ def test_qwen2_two_layers_benchmark_distribution():
     cfg = synthetic.qwen2_1_5b(num_hidden_layers=2)
     cos, _ = _run(cfg, synthetic.awq_weights(cfg, seed=0, norm_noise=0.1), [16, 100, 511, 7])
     assert cos.min() >= 0.998, cos
+
+
+def test_cuda_graph_replay_matches_eager_for_new_batches():
+    # One captured forward serves every batch of the same token count: the device
+    # schedule (sequence starts, attention work list) is recomputed inside the graph.
+    cfg = synthetic.qwen3_0_6b(num_hidden_layers=2)
+    weights = synthetic.awq_weights(cfg, seed=0, device="cuda:0")
+    worker = GPUWorker(MESConfig(model_config=cfg), device="cuda:0")
+    load_weights(worker.model, weights)
+    for i, lengths in enumerate([[300, 500, 200], [100, 900], [1000], [1] * 10 + [990]]):
+        ids, pos, last = synthetic.packed_batch(lengths, cfg.vocab_size, seed=i)
+        worker.use_cuda_graphs = True
+        got = worker.embed(ids, pos, last).numpy()
+        worker.use_cuda_graphs = False
+        want = worker.embed(ids, pos, last).numpy()
+        assert np.array_equal(got, want), lengths
+    assert len(worker._graphs) == 1 and not worker._no_graph
+    assert _C.take_device_error() == 0
