@@ -37,10 +37,11 @@ sys.path.insert(0, ROOT)
 METRIC = "embedding tokens/sec (20x1000-tok batch)"
 
 # DRAM bytes (read + write) of one launch, from `ncu --set full` captures of the same
-# command (profiles/awq_gemm_gate_up_20000x6144x1024.md); None where not captured.
+# command (profiles/awq_gemm_silu_gate_up_20000x6144x1024.md and
+# profiles/awq_gemm_pair_o_proj_20000x1024x2048.md); None where not captured.
 MEASURED_TRAFFIC: dict = {
-    ("bf16", 20000, 6144, 1024): 239.1e6,       # gate_up, layer 0
-    ("residual", 20000, 1024, 3072): 259.1e6,   # down_proj, layer 0
+    ("silu", 20000, 6144, 1024): 117.3e6,       # gate_up + SiLU-and-mul, layer 0
+    ("residual", 20000, 1024, 2048): 205.7e6,   # o_proj (CTA pairs), layer 0
 }
 UNIT = "tokens/s"
 
