@@ -50,7 +50,7 @@ def _worker(rank, port, q):
     from mes_b200 import _C
     from mes_b200.core.gpu_worker import tp_nccl_environment
     from mes_b200.models.qwen2 import DecoderModel
-    tp_nccl_environment()
+    tp_nccl_environment(2)
     dist.init_process_group("nccl", rank=rank, world_size=2, device_id=dev,
                             timeout=datetime.timedelta(seconds=60))
     try:
