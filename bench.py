@@ -52,7 +52,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["mes", "reference"], default="mes")
-    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "ew"], default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -417,12 +417,83 @@ def run_gemm_micro(args):
             del x, y
 
 
+def run_elementwise_micro(args):
+    """The memory-bound kernels of the forward at the 20 x 1000-token shapes of the
+    Qwen3-0.6B workload (T = 20000, H = 1024, 16 q / 8 kv heads of 128, I = 3072), one JSON
+    line per kernel: algorithmic HBM bytes per launch / CUDA-event time, against the HBM
+    peak.  Each launch is timed alone after a 256 MB write that evicts L2."""
+    import numpy as np
+    import torch
+    import __graft_entry__
+    __graft_entry__.build()
+    from mes_b200 import _C, synthetic
+    from mes_b200.layers.rotary_embedding import RotaryEmbedding
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _, _, hbm, peak_kind = peaks()
+    g = torch.Generator(device=dev).manual_seed(0)
+    T, H, Hq, Hkv, D, I, V = 20000, 1024, 16, 8, 128, 3072, 151669
+    _, pos_np, last_np = synthetic.packed_batch([1000] * 20, V, seed=1)
+    pos = torch.from_numpy(pos_np).to(dev)
+    last = torch.from_numpy(last_np).to(dev)
+    ids = torch.randint(0, V, (T,), generator=g, device=dev)
+    table = torch.randn(V, H, generator=g, device=dev).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(H, generator=g, device=dev)).to(torch.bfloat16)
+    wd = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).to(torch.bfloat16)
+    res = torch.randn(T, H, generator=g, device=dev)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, generator=g, device=dev).to(torch.bfloat16)
+    cache = RotaryEmbedding(D, D, 32768, 1e6).cos_sin_cache.to(dev)   # the model's fp32 table
+    gu = torch.randn(T, 2 * I, generator=g, device=dev).to(torch.bfloat16)
+    act = torch.empty(T, I, dtype=torch.bfloat16, device=dev)
+    emb = torch.empty(T, H, dtype=torch.float32, device=dev)
+    cases = [
+        ("rmsnorm (fp32 residual in, bf16 out)", lambda: _C.rmsnorm(res, w, 1e-6, out),
+         T * H * 4 + T * H * 2),
+        ("add + rmsnorm (bf16 delta into the fp32 residual)",
+         lambda: _C.add_rmsnorm_f32res(x, res, w, 1e-6, out), T * H * (2 + 8 + 2)),
+        ("q/k rmsnorm + rope (in place, 16 q + 8 k heads)",
+         lambda: _C.qknorm_rope(qkv, pos, cache, Hq, Hkv, D, wd, wd),
+         2 * T * (Hq + Hkv) * D * 2 + T * 8),
+        ("silu-and-mul (standalone)", lambda: _C.silu_mul(gu, act), T * I * 2 * 2 + T * I * 2),
+        ("embedding gather (fp32 out)", lambda: _C.embedding_f32(ids, table, emb),
+         T * H * 2 + T * 8 + T * H * 4),
+        ("last token + L2 (20 rows)", lambda: _C.last_token_l2(out, last), 20 * H * 2 + 20 * H * 4),
+        ("varlen schedule (20 sequences)", lambda: _C.varlen_schedule(pos), T * 8 + 4 * (T + 1)),
+    ]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for name, fn, nbytes in cases:
+        times = []
+        for it in range(args.warmup + args.steps):
+            flush.fill_(it & 0xFF)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            if it >= args.warmup:
+                times.append(e0.elapsed_time(e1) / 1000.0)
+        t = statistics.median(times)
+        gbs = nbytes / t / 1e9
+        print(json.dumps({
+            "metric": "HBM GB/s (algorithmic bytes)", "kernel": name, "value": gbs,
+            "unit": "GB/s", "us": t * 1e6, "bytes": nbytes, "steps": args.steps,
+            "frac_of_hbm_peak": gbs / hbm, "peak": hbm, "peak_kind": f"{peak_kind} HBM copy",
+            "l2": "256 MB written between launches"}), flush=True)
+    if _C.take_device_error():
+        raise RuntimeError("device error in the elementwise benchmark")
+
+
 def main():
     args = parse_args()
     import __graft_entry__
     __graft_entry__.load_package()
     if args.workload == "c3" and args.impl == "mes":
         run_gemm_micro(args)
+        return
+    if args.workload == "ew" and args.impl == "mes":
+        run_elementwise_micro(args)
         return
     if args.impl == "reference":
         run_reference(args)

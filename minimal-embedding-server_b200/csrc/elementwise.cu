@@ -122,11 +122,12 @@ __global__ void rmsnorm_kernel(const XT* x, const RT* residual, const uint4* __r
 }
 
 // ------------------------------ q/k RMSNorm + NeoX RoPE --------------------------------
-// 16 threads per (token, group of 4 heads): thread j owns elements 8j..8j+7 of each 128-wide
-// head, so the token's cos/sin values and the norm weights are loaded once per 4 heads and
-// the four heads' loads are in flight together.  Units are token-major, so a block covers
-// consecutive kilobytes of the packed qkv rows; the small units keep the grid at several
-// waves of the GPU.  The rotate-half partner of thread j is j ^ 8.
+// 16 threads per (token, group of kGroupHeads heads): thread j owns elements 8j..8j+7 of
+// each 128-wide head, so the token's cos/sin values and the norm weights are loaded once
+// per group and the group's head loads are all in flight together (kGroupHeads x 16 bytes
+// per thread).  Units are token-major, so a block covers consecutive kilobytes of the
+// packed qkv rows.  The rotate-half partner of thread j is j ^ 8.
+constexpr int kGroupHeads = 8;
 template <bool kF32Cache>
 __device__ __forceinline__ void load_cos_sin(const void* cos_sin, int64_t ps, int cj, float (&c)[8],
                                              float (&s)[8]) {
@@ -144,17 +145,22 @@ __device__ __forceinline__ void load_cos_sin(const void* cos_sin, int64_t ps, in
 }
 
 template <bool kNorm, bool kF32Cache>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 3)
 qknorm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, const int64_t* __restrict__ pos,
                    const void* __restrict__ cos_sin, int64_t max_pos, const uint4* __restrict__ qw,
                    const uint4* __restrict__ kw, int T, int Hq, int Hkv, float eps) {
   const int nh = Hq + Hkv;
-  const int ngroups = (nh + 3) >> 2;
+  const int ngroups = (nh + kGroupHeads - 1) / kGroupHeads;
   const int unit = blockIdx.x * 16 + (threadIdx.x >> 4);
   const int j = threadIdx.x & 15;
   const bool valid = unit < T * ngroups;
   const int t = valid ? unit / ngroups : 0;
-  const int h0 = (unit - t * ngroups) * 4;
+  const int h0 = (unit - t * ngroups) * kGroupHeads;
+  uint4* row = reinterpret_cast<uint4*>(qkv + (int64_t)t * ld) + h0 * 16 + j;
+  uint4 raw[kGroupHeads];
+#pragma unroll
+  for (int u = 0; u < kGroupHeads; ++u)
+    raw[u] = (valid && h0 + u < nh) ? row[u * 16] : make_uint4(0, 0, 0, 0);
   int64_t ps = valid ? __ldg(pos + t) : 0;
   if (ps < 0 || ps >= max_pos) {
     if (valid && j == 0 && h0 == 0) atomicCAS(&g_err_elementwise, 0, MES_ERR_INVALID);
@@ -162,20 +168,16 @@ qknorm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, const int64_t* _
   }
   float c[8], s[8];
   load_cos_sin<kF32Cache>(cos_sin, ps, (j & 7) * 8, c, s);
-  float wq[8], wk[8];
+  uint4 wq = make_uint4(0, 0, 0, 0), wk = make_uint4(0, 0, 0, 0);  // unpacked per head
   if (kNorm) {
-    unpack8(h0 < Hq ? __ldg(qw + j) : make_uint4(0, 0, 0, 0), wq);
-    unpack8(Hkv > 0 && h0 + 4 > Hq ? __ldg(kw + j) : make_uint4(0, 0, 0, 0), wk);
+    if (h0 < Hq) wq = __ldg(qw + j);
+    if (Hkv > 0 && h0 + kGroupHeads > Hq) wk = __ldg(kw + j);
   }
-  uint4* row = reinterpret_cast<uint4*>(qkv + (int64_t)t * ld) + h0 * 16 + j;
-  uint4 raw[4];
 #pragma unroll
-  for (int u = 0; u < 4; ++u)
-    raw[u] = (valid && h0 + u < nh) ? row[u * 16] : make_uint4(0, 0, 0, 0);
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    // Every lane runs all four heads (the two units of a warp may differ in head count and
-    // the shuffles use the full mask); heads past the end compute on zeros and store nothing.
+  for (int u = 0; u < kGroupHeads; ++u) {
+    // Every lane runs all the group's heads (the two units of a warp may differ in head
+    // count and the shuffles use the full mask); heads past the end compute on zeros and
+    // store nothing.
     float f[8];
     unpack8(raw[u], f);
     if (kNorm) {
@@ -185,9 +187,10 @@ qknorm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, const int64_t* _
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       const float rs = rsqrtf(ss * (1.0f / 128.0f) + eps);
-      const bool is_q = h0 + u < Hq;
+      float wf[8];
+      unpack8(h0 + u < Hq ? wq : wk, wf);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) f[i] = round_bf16(round_bf16(f[i] * rs) * (is_q ? wq[i] : wk[i]));
+      for (int i = 0; i < 8; ++i) f[i] = round_bf16(round_bf16(f[i] * rs) * wf[i]);
     }
     float o[8];
 #pragma unroll
@@ -390,10 +393,12 @@ static int launch_rmsnorm(const void* x, const void* residual, const void* w, vo
       (kAdd && (!aligned16(residual) || !aligned16(residual_out))))
     return MES_ERR_ALIGN;
   if (rows > 0x7fffffffLL) return MES_ERR_INVALID;
+  cudaStream_t s = (cudaStream_t)stream;
+  const float inv_h = 1.0f / (float)H;
   const int hv = (int)(H / 8);
-  rmsnorm_kernel<XT, RT, kAdd><<<(unsigned)rows, hv, 0, (cudaStream_t)stream>>>(
+  rmsnorm_kernel<XT, RT, kAdd><<<(unsigned)rows, hv, 0, s>>>(
       (const XT*)x, (const RT*)residual, (const uint4*)w, (__nv_bfloat16*)y, (RT*)residual_out, hv,
-      1.0f / (float)H, eps);
+      inv_h, eps);
   return mes_host::from_cuda(cudaGetLastError());
 }
 
@@ -432,7 +437,7 @@ extern "C" int mes_qknorm_rope(void* qkv, int64_t ld, const int64_t* positions,
   if (apply_norm && ((Hq > 0 && !q_w) || (Hkv > 0 && !k_w))) return MES_ERR_INVALID;
   if (!aligned16(qkv) || !aligned16(cos_sin) || (apply_norm && (!aligned16(q_w) || !aligned16(k_w))))
     return MES_ERR_ALIGN;
-  const int64_t units = T * (((int64_t)Hq + Hkv + 3) / 4);
+  const int64_t units = T * (((int64_t)Hq + Hkv + kGroupHeads - 1) / kGroupHeads);
   if (units > 0x7fffffffLL - 16) return MES_ERR_INVALID;
   const unsigned blocks = (unsigned)((units + 15) / 16);
   cudaStream_t s = (cudaStream_t)stream;
