@@ -88,16 +88,32 @@ def _worker(rank, world, port, arch, result_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("arch", ["qwen3", "qwen2"])
-def test_tp2_shards_reproduce_tp1(arch):
+@pytest.mark.parametrize("arch,world", [("qwen3", 2), ("qwen2", 2), ("qwen3", 4), ("qwen3", 8)])
+def test_tp_shards_reproduce_tp1(arch, world):
+    # Qwen3-0.6B at TP 4 / 8: 4 / 2 q heads and 2 / 1 kv heads per rank; down_proj's K
+    # shard is 768 / 384 (6 / 3 AWQ groups).
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, arch, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, arch, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    results = dict(q.get(timeout=10) for _ in range(2))
+    results = dict(q.get(timeout=10) for _ in range(world))
     assert max(results.values()) < 1e-5, results
+
+
+def test_overlap_split_is_a_sequence_start_near_the_middle(monkeypatch):
+    import numpy as np
+    from mes_b200.models import qwen2
+    monkeypatch.setattr(qwen2, "_tp_size", lambda: 2)
+    pos = np.concatenate([np.arange(n) for n in (1000, 700, 1300, 1000, 1000)])
+    assert qwen2.DecoderModel.overlap_split_host(pos) == 3000     # starts 1000, 1700, 3000, 4000
+    assert qwen2.DecoderModel.overlap_split_host(np.arange(5000)) is None       # one sequence
+    assert qwen2.DecoderModel.overlap_split_host(np.arange(100)) is None        # below the threshold
+    monkeypatch.setattr(qwen2, "_tp_size", lambda: 1)
+    assert qwen2.DecoderModel.overlap_split_host(pos) is None                  # tp == 1
+    assert qwen2.DecoderModel.overlap_reserved_sms(2) == 16
+    assert qwen2.DecoderModel.overlap_reserved_sms(8) == 32
