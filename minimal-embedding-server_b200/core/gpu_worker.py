@@ -37,13 +37,10 @@ def tp_nccl_environment(world_size: int | None = None) -> None:
     """Call before ``init_process_group`` at tensor parallelism > 1 (``world_size``
     defaults to ``WORLD_SIZE``).  The model overlaps each all-reduce with the other
     micro-batch's kernels and keeps ``DecoderModel.overlap_reserved_sms(world_size)`` SMs
-    free for it; capping NCCL's channels (one CTA each, ring/tree and NVLink SHARP alike)
-    at as many keeps the collective inside them.  Settings already in the environment
-    win."""
+    free for it; capping NCCL's ring/tree channels (one CTA each) at as many keeps the
+    collective inside them.  Settings already in the environment win."""
     world = int(world_size if world_size is not None else os.environ.get("WORLD_SIZE", "1"))
-    sms = str(max(DecoderModel.overlap_reserved_sms(world), 1))
-    os.environ.setdefault("NCCL_MAX_NCHANNELS", sms)
-    os.environ.setdefault("NCCL_NVLS_NCHANNELS", sms)
+    os.environ.setdefault("NCCL_MAX_NCHANNELS", str(max(DecoderModel.overlap_reserved_sms(world), 1)))
 
 
 class GPUWorker:
