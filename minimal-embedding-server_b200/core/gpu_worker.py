@@ -23,6 +23,7 @@ from __future__ import annotations
 
 import collections
 import os
+import warnings
 
 import numpy as np
 import torch
@@ -96,7 +97,9 @@ class GPUWorker:
             return g
         try:
             g = self.capture(key[0], key[1], input_ids, positions)
-        except Exception:   # an unsupported capture runs eagerly from now on
+        except Exception as exc:   # an unsupported capture runs eagerly from now on
+            warnings.warn(f"CUDA-graph capture of a {key[0]}-token batch failed ({exc!r}); "
+                          "batches of this shape run eagerly", RuntimeWarning, stacklevel=2)
             self._no_graph.add(key)
             return None
         self._graphs[key] = g
