@@ -373,10 +373,40 @@ def run_mes(args):
     return result
 
 
+COLD_L2 = ("before each launch 256 MB written, then another 256 MB read (L2 cold and clean); "
+           "the launch is queued behind a GPU spin, so no host gap is timed")
+
+
+def cold_launch_time(fn, args, dev) -> float:
+    """Median CUDA-event time (s) of one launch of ``fn`` with a cold L2.  Before each launch
+    a 256 MB buffer is written (the L2 flush) and a second 256 MB buffer read, which evicts
+    the written lines so that their write-back is not timed; then the GPU spins for ~0.5 ms
+    while the host queues the events and the launch, so the host's launch cost is not
+    timed either."""
+    import torch
+    if not hasattr(cold_launch_time, "bufs"):
+        cold_launch_time.bufs = (torch.empty(256 << 20, dtype=torch.uint8, device=dev),
+                                 torch.ones(32 << 20, dtype=torch.int64, device=dev))
+    wbuf, rbuf = cold_launch_time.bufs
+    times = []
+    for it in range(args.warmup + args.steps):
+        wbuf.fill_(it & 0xFF)
+        rbuf.sum()
+        torch.cuda._sleep(1_000_000)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        if it >= args.warmup:
+            times.append(e0.elapsed_time(e1) / 1000.0)
+    return statistics.median(times)
+
+
 def run_gemm_micro(args):
     """AWQ W4A16 GEMM microbenchmark on the Qwen3-Embedding-4B projection shapes (one JSON
-    line per shape and M).  Each launch is timed alone with CUDA events after a 256 MB
-    write that evicts L2; the bound is min(tensor peak, arithmetic intensity x HBM)."""
+    line per shape and M).  Each launch is timed alone with CUDA events and a cold L2
+    (``cold_launch_time``); the bound is min(tensor peak, arithmetic intensity x HBM)."""
     import torch
     import __graft_entry__
     __graft_entry__.build()
@@ -385,7 +415,6 @@ def run_gemm_micro(args):
     torch.cuda.set_device(dev)
     peak_burst, _, hbm, peak_kind = peaks()
     shapes = {"qkv": (2560, 6144), "o": (4096, 2560), "gate_up": (2560, 19456), "down": (9728, 2560)}
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     gen = torch.Generator(device=dev).manual_seed(0)
     for name, (K, N) in shapes.items():
         qw, qz, sc = synthetic.random_awq(K, N, gen, dev)
@@ -393,17 +422,7 @@ def run_gemm_micro(args):
         for M in (16, 256, 2048, 20000, 120000):
             x = torch.randn(M, K, generator=gen, device=dev).to(torch.bfloat16)
             y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
-            times = []
-            for it in range(args.warmup + args.steps):
-                flush.fill_(it & 0xFF)
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                _C.awq_gemm(x, qwm, qz, sc16, None, y)
-                e1.record()
-                torch.cuda.synchronize()
-                if it >= args.warmup:
-                    times.append(e0.elapsed_time(e1) / 1000.0)
-            t = statistics.median(times)
+            t = cold_launch_time(lambda: _C.awq_gemm(x, qwm, qz, sc16, None, y), args, dev)
             flops = 2.0 * M * N * K
             nbytes = K * N / 2 + (K // 128) * N * 2.5 + 2 * M * K + 2 * M * N
             bound_tflops = min(peak_burst, flops / nbytes * hbm * 1e9 / 1e12)
@@ -413,7 +432,7 @@ def run_gemm_micro(args):
                 "value": tf, "unit": "TFLOP/s", "us": t * 1e6, "steps": args.steps,
                 "frac_of_tensor_peak": tf / peak_burst, "bound": "tensor" if bound_tflops >= peak_burst else "hbm",
                 "frac_of_bound": tf / bound_tflops, "peak_kind": f"{peak_kind} bf16 burst",
-                "l2": "256 MB written between launches"}), flush=True)
+                "l2": COLD_L2}), flush=True)
             del x, y
 
 
@@ -421,7 +440,7 @@ def run_elementwise_micro(args):
     """The memory-bound kernels of the forward at the 20 x 1000-token shapes of the
     Qwen3-0.6B workload (T = 20000, H = 1024, 16 q / 8 kv heads of 128, I = 3072), one JSON
     line per kernel: algorithmic HBM bytes per launch / CUDA-event time, against the HBM
-    peak.  Each launch is timed alone after a 256 MB write that evicts L2."""
+    peak.  Each launch is timed alone with a cold L2 (``cold_launch_time``)."""
     import numpy as np
     import torch
     import __graft_entry__
@@ -462,25 +481,14 @@ def run_elementwise_micro(args):
         ("last token + L2 (20 rows)", lambda: _C.last_token_l2(out, last), 20 * H * 2 + 20 * H * 4),
         ("varlen schedule (20 sequences)", lambda: _C.varlen_schedule(pos), T * 8 + 4 * (T + 1)),
     ]
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     for name, fn, nbytes in cases:
-        times = []
-        for it in range(args.warmup + args.steps):
-            flush.fill_(it & 0xFF)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            fn()
-            e1.record()
-            torch.cuda.synchronize()
-            if it >= args.warmup:
-                times.append(e0.elapsed_time(e1) / 1000.0)
-        t = statistics.median(times)
+        t = cold_launch_time(fn, args, dev)
         gbs = nbytes / t / 1e9
         print(json.dumps({
             "metric": "HBM GB/s (algorithmic bytes)", "kernel": name, "value": gbs,
             "unit": "GB/s", "us": t * 1e6, "bytes": nbytes, "steps": args.steps,
             "frac_of_hbm_peak": gbs / hbm, "peak": hbm, "peak_kind": f"{peak_kind} HBM copy",
-            "l2": "256 MB written between launches"}), flush=True)
+            "l2": COLD_L2}), flush=True)
     if _C.take_device_error():
         raise RuntimeError("device error in the elementwise benchmark")
 

@@ -123,66 +123,102 @@ __device__ __forceinline__ uint32_t dq_pair(uint32_t w, const GroupParams& g) {
 }
 
 // ----------------------------------------------------------------------------------------
-// BT tokens per tile (the MMA's N), STAGES pipeline stages, NDQ dequant/epilogue warps
-// (4: one per TMEM lane quadrant; 8: two per quadrant, each taking half of a stage's
-// words and half of the epilogue's token chunks).
-template <int BT, int STAGES, int EPI, int NDQ>
+// One tile per CTA (small M): BT tokens (the MMA's N), STAGES shared-memory stages, ASLOTS
+// dequantised-A slots in TMEM, NDQ dequant/epilogue warps (4: one per TMEM lane quadrant;
+// 8: two per quadrant, each taking half of a stage's words and half of the epilogue's token
+// chunks).  Each stage holds the X tile, the packed weight words and the group's scales and
+// zero words (all by TMA).  Small tiles stream little data per k-step, so the ring is deep
+// (about 100 KB in flight per CTA) to cover the HBM latency, while TMEM keeps only a few A
+// slots.
+//
+// Split-K over a cluster.  With split > 1 the grid is launched in clusters of `split` CTAs
+// along x, all on the same 128-feature x BT-token tile; CTA r runs the weight groups
+// [r G / split, (r + 1) G / split) of the G = K / 128 groups.  After the mainloop each CTA
+// writes its fp32 partial tile into its stage ring (idle by then), the cluster
+// synchronises, and the tile's (lane quadrant, token chunk) units are dealt out over the
+// cluster: the CTA owning a unit reads that unit of all `split` partial tiles through
+// distributed shared memory, adds them in rank order (so the sum does not depend on which
+// CTA reduces) and runs the epilogue.  A second cluster barrier keeps every CTA's shared
+// memory alive until all reads are done.  No global workspace and no atomics: the result
+// is deterministic.
+template <int BT, int STAGES, int ASLOTS, int EPI, int NDQ>
 struct Cfg {
   static constexpr bool kResidual = EPI == kEpiResidual, kSilu = EPI == kEpiSilu;
   static constexpr int kThreads = 64 + 32 * NDQ;  // warp 0 TMA, warp 1 MMA, then NDQ warps
   static constexpr int kHalves = NDQ / 4;
   static constexpr int kWords = 8 / kHalves;      // packed words per dequant thread per stage
   static constexpr int kXStage = BT * kBK * 2;
-  static constexpr int kWStage = (kBK / 8) * kBN * 4;
+  static constexpr int kWBytes = (kBK / 8) * kBN * 4;  // 8 words x 128 features
+  static constexpr int kWStage = kWBytes + 256 + 128;  // words | scales (256 B) | zeros (64 B)
   static constexpr int kChunk = kResidual ? 16 : (BT < 32 ? BT : 32);  // tokens per epilogue step
   static constexpr int kOutBuf = kChunk * 32 * 2;  // one staging block per epilogue warp
   static constexpr int kOffX = 0;
   static constexpr int kOffW = STAGES * kXStage;
   static constexpr int kOffOut = kOffW + STAGES * kWStage;
   static constexpr int kOffBar = kOffOut + (kResidual ? 0 : NDQ * kOutBuf);
-  static constexpr int kSmem = kOffBar + 256 + 1024;  // barriers + 1 KB alignment slack
-  static constexpr int kTmemNeed = BT + STAGES * 32;
+  static constexpr int kSmem = kOffBar + 512 + 1024;  // barriers + 1 KB alignment slack
+  static constexpr int kRedBytes = BT * kBN * 4;      // one fp32 partial tile (split-K)
+  static constexpr int kTmemNeed = BT + ASLOTS * 32;
   static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64
                                  : kTmemNeed <= 128 ? 128 : kTmemNeed <= 256 ? 256 : 512;
+  // Shared memory requested at launch: at least enough that no more CTAs fit on an SM
+  // (228 KB, 1 KB reserved per CTA) than its 512 TMEM columns serve at once, so that no CTA
+  // waits in tcgen05.alloc for another; with split-K such a wait could close a cycle
+  // through the cluster barriers.  The launcher checks the resulting occupancy.
+  static constexpr int kCtasByTmem = 512 / kTmemCols;
+  static constexpr int kSmemFloor = 233472 / (kCtasByTmem + 1) - 1024 + 1;
+  static constexpr int kSmemLaunch = kSmem > kSmemFloor ? kSmem : kSmemFloor;
   static_assert(NDQ == 4 || NDQ == 8, "dequant warps");
   static_assert(kTmemNeed <= 512, "TMEM budget");
+  static_assert(kSmemLaunch <= 232448, "shared memory budget");
   static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N");
-  static_assert(kXStage % 1024 == 0, "swizzle atoms");
+  static_assert(kXStage % 1024 == 0 && kWStage % 128 == 0, "stage alignment");
+  static_assert(kRedBytes <= kOffOut, "the partial tile fits in the stage ring");
+  static_assert((2 * STAGES + 2 * ASLOTS + 1) * 8 + 8 <= 512, "barrier area");
+  static_assert(kChunk % 4 == 0, "partial tiles are stored four tokens per 16 bytes");
 };
 
 // EPI selects the epilogue (kEpiBf16 / kEpiResidual / kEpiSilu, see their definition).
-template <int BT, int STAGES, int EPI, int NDQ>
-__global__ void __launch_bounds__(Cfg<BT, STAGES, EPI, NDQ>::kThreads)
+template <int BT, int STAGES, int ASLOTS, int EPI, int NDQ>
+__global__ void __launch_bounds__(Cfg<BT, STAGES, ASLOTS, EPI, NDQ>::kThreads)
 awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                const __grid_constant__ CUtensorMap map_y, const int32_t* __restrict__ qzeros,
-                const uint16_t* __restrict__ scales, const __nv_bfloat16* __restrict__ bias,
-                float* __restrict__ R, int64_t ldr, int M, int N, int K) {
-  using C = Cfg<BT, STAGES, EPI, NDQ>;
+                const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
+                const __grid_constant__ CUtensorMap map_y, const __nv_bfloat16* __restrict__ bias,
+                float* __restrict__ R, int64_t ldr, int M, int N, int K, int split) {
+  using C = Cfg<BT, STAGES, ASLOTS, EPI, NDQ>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xs = smem + C::kOffX;
-  const uint32_t* ws = reinterpret_cast<const uint32_t*>(smem + C::kOffW);
+  uint8_t* wst = smem + C::kOffW;
+  float* red = reinterpret_cast<float*>(smem);  // partial tile over the ring (split > 1)
   __nv_bfloat16* outbuf = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffOut);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
-  uint64_t* full = bars;                  // TMA landed (X + W words)
-  uint64_t* afull = bars + STAGES;        // dequantised A written to TMEM
-  uint64_t* empty = bars + 2 * STAGES;    // MMAs of the stage done
-  uint64_t* accum = bars + 3 * STAGES;    // all MMAs done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 1);
+  uint64_t* full = bars;                  // [STAGES] TMA landed (X, words, scales, zeros)
+  uint64_t* empty = bars + STAGES;        // [STAGES] MMAs of the stage done
+  uint64_t* afull = bars + 2 * STAGES;    // [ASLOTS] dequantised A written to TMEM
+  uint64_t* aempty = afull + ASLOTS;      // [ASLOTS] MMAs reading the A slot done
+  uint64_t* accum = aempty + ASLOTS;      // all MMAs done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-
   const int warp = mes::warp_id(), lane = mes::lane_id();
-  const int n0 = blockIdx.x * kBN;
+  const int rank = split > 1 ? static_cast<int>(mes::cluster_ctarank()) : 0;
+  const int n0 = (blockIdx.x / split) * kBN;
   const int t0 = blockIdx.y * BT;
-  const int nk = K / kBK;
+  // This CTA's k-steps: whole groups (two 64-k steps each), split as evenly as they go.
+  const int groups = K / kGroup;
+  const int kb0 = 2 * (rank * groups / split);
+  const int nloc = 2 * ((rank + 1) * groups / split) - kb0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mes::mbar_init(&full[s], 1);
-      mes::mbar_init(&afull[s], NDQ);
       mes::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < ASLOTS; ++a) {
+      mes::mbar_init(&afull[a], NDQ);
+      mes::mbar_init(&aempty[a], 1);
     }
     mes::mbar_init(accum, 1);
     *abort_flag = 0;
@@ -191,6 +227,8 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
   if (warp == 0 && lane == 0) {
     mes::tma_prefetch_desc(&map_x);
     mes::tma_prefetch_desc(&map_w);
+    mes::tma_prefetch_desc(&map_s);
+    mes::tma_prefetch_desc(&map_z);
     if (!C::kResidual) mes::tma_prefetch_desc(&map_y);
   }
   if (warp == 1) {
@@ -202,27 +240,77 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
   __syncthreads();
   mes::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_a = tmem + BT;  // A stages after the BT accumulator columns
+  const uint32_t tmem_a = tmem + BT;  // A slots after the BT accumulator columns
 
+  // Epilogue of one chunk of C::kChunk tokens at token offset c0 of the tile, for the 32
+  // features of lane quadrant q (v[j] = fp32 bits of token c0 + j, feature of this lane).
+  const int q = warp & 3;
+  const int row = q * 32 + lane;  // feature within the tile (dequant / epilogue warps)
+  const int n = n0 + row;
+  const float bv = (warp >= 2 && bias) ? __bfloat162float(bias[n]) : 0.f;
+  __nv_bfloat16* buf = outbuf + (warp >= 2 ? warp - 2 : 0) * (C::kOutBuf / 2);
+  bool stored = false;
+  auto store_chunk = [&](const uint32_t (&v)[C::kChunk], int c0) {
+    if constexpr (C::kSilu) {
+      silu_chunk<C::kChunk>(v, lane, buf, stored, &map_y, n0 / 2 + q * 16, t0 + c0);
+    } else if constexpr (C::kResidual) {
+      // Each lane owns feature n; a warp touches 32 consecutive fp32 per token row.
+      const int rows = min(C::kChunk, M - (t0 + c0));
+      float* rp = R + (int64_t)(t0 + c0) * ldr + n;
+      float rv[C::kChunk];
+#pragma unroll
+      for (int j = 0; j < C::kChunk; ++j) rv[j] = j < rows ? rp[(int64_t)j * ldr] : 0.f;
+#pragma unroll
+      for (int j = 0; j < C::kChunk; ++j)
+        if (j < rows) rp[(int64_t)j * ldr] = rv[j] + (__uint_as_float(v[j]) + bv);
+    } else {
+      if (stored) {  // the previous TMA store must have read the staging block
+        if (lane == 0) mes::tma_store_wait_read<0>();
+        __syncwarp();
+      }
+#pragma unroll
+      for (int j = 0; j < C::kChunk; ++j)
+        buf[j * 32 + lane] = __float2bfloat16_rn(__uint_as_float(v[j]) + bv);
+      mes::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mes::tma_store_2d(&map_y, buf, n0 + q * 32, t0 + c0);
+        mes::tma_store_commit();
+      }
+      __syncwarp();
+      stored = true;
+    }
+  };
+  auto load_acc = [&](uint32_t (&v)[C::kChunk], int c0) {
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    if constexpr (C::kChunk == 32) mes::tmem_ld32(tmem + lane_off + c0, v);
+    else mes::tmem_ld16(tmem + lane_off + c0, v);
+    mes::tmem_wait_ld();
+  };
+
+  bool epi_ok = false;  // this warp's accumulator is complete (dequant / epilogue warps)
   if (warp == 0) {
     // ------------------------------- TMA producer -------------------------------------
     if (lane == 0) {
       int issued = 0;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        if (kb >= STAGES &&
-            !mes::mbar_wait(&empty[s], ((kb / STAGES) & 1) ^ 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT))
+      for (int i = 0; i < nloc; ++i) {
+        const int s = i % STAGES, kb = kb0 + i;
+        if (i >= STAGES &&
+            !mes::mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT))
           break;
-        mes::mbar_arrive_expect_tx(&full[s], C::kXStage + C::kWStage);
+        uint8_t* w = wst + s * C::kWStage;
+        mes::mbar_arrive_expect_tx(&full[s], C::kXStage + C::kWBytes + 256 + 64);
         mes::tma_load_2d(xs + s * C::kXStage, &map_x, &full[s], kb * kBK, t0);
-        mes::tma_load_2d((void*)(ws + s * (C::kWStage / 4)), &map_w, &full[s], n0, kb * (kBK / 8));
-        issued = kb + 1;
+        mes::tma_load_2d(w, &map_w, &full[s], n0, kb * (kBK / 8));
+        mes::tma_load_2d(w + C::kWBytes, &map_s, &full[s], n0, kb / 2);
+        mes::tma_load_2d(w + C::kWBytes + 256, &map_z, &full[s], n0 / 8, kb / 2);
+        issued = i + 1;
       }
       if (*abort_flag) {
         // Let the copies already issued land before the CTA exits.
-        for (int kb = issued - STAGES < 0 ? 0 : issued - STAGES; kb < issued; ++kb) {
+        for (int i = issued - STAGES < 0 ? 0 : issued - STAGES; i < issued; ++i) {
           const uint64_t tstart = mes::globaltimer_ns();
-          while (!mes::mbar_try_wait(&full[kb % STAGES], (kb / STAGES) & 1) &&
+          while (!mes::mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) &&
                  mes::globaltimer_ns() - tstart < mes::kWaitLimitNs) {
           }
         }
@@ -234,19 +322,20 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
     if (lane == 0) {
       constexpr uint32_t idesc = mes::idesc_bf16_f32(kBN, BT, false);
       const uint32_t xs_addr = mes::smem_u32(xs);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mes::mbar_wait(&full[s], ph, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) break;
-        if (!mes::mbar_wait(&afull[s], ph, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) break;
+      for (int i = 0; i < nloc; ++i) {
+        const int s = i % STAGES, a = i % ASLOTS;
+        // afull implies full: every dequant warp waited for the whole stage (X included)
+        // before arriving.
+        if (!mes::mbar_wait(&afull[a], (i / ASLOTS) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) break;
         mes::tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
           const uint64_t bdesc =
               mes::smem_desc_sw128(xs_addr + s * C::kXStage + kk * 32, 16, 1024);
-          mes::mma_ts(tmem, tmem_a + s * 32 + kk * 8, bdesc, idesc, (kb | kk) != 0);
+          mes::mma_ts(tmem, tmem_a + a * 32 + kk * 8, bdesc, idesc, (i | kk) != 0);
         }
         mes::tc_commit(&empty[s]);
+        mes::tc_commit(&aempty[a]);
       }
       mes::tc_commit(accum);
       if (*abort_flag) {
@@ -258,96 +347,107 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
     __syncwarp();
   } else if (warp < 2 + NDQ) {
     // --------------------------- dequant + epilogue warps -----------------------------
-    const int q = warp & 3;                 // TMEM lane quadrant of this warp
     const int half = (warp - 2) / 4;        // which half of the words / token chunks
-    const int row = q * 32 + lane;          // feature within the tile
-    const int n = n0 + row;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    const int zshift = 4 * kInvOrder[n & 7];
-    const int NW = N >> 3;
-    // Group parameters: raw values of the next group are loaded one group ahead.
-    uint32_t zraw = __ldg(qzeros + (n >> 3));
-    uint16_t sraw = __ldg(scales + n);
-    GroupParams gp = make_group(zraw, zshift, sraw);
+    const int zshift = 4 * kInvOrder[row & 7];  // n0 is a multiple of 128
     bool ok = true;
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t ph = (kb / STAGES) & 1;
-      if ((kb & 1) == 0) {  // a new 128-wide group starts every other stage
-        gp = make_group(zraw, zshift, sraw);
-        const int gn = (kb >> 1) + 1;
-        if (gn < K / kGroup) {
-          zraw = __ldg(qzeros + (int64_t)gn * NW + (n >> 3));
-          sraw = __ldg(scales + (int64_t)gn * N + n);
-        }
+    for (int i = 0; i < nloc; ++i) {
+      const int s = i % STAGES, a = i % ASLOTS;
+      if (!mes::mbar_wait_warp(&full[s], (i / STAGES) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT) ||
+          (i >= ASLOTS &&
+           !mes::mbar_wait_warp(&aempty[a], ((i / ASLOTS) & 1) ^ 1, abort_flag, &g_err_gemm,
+                                MES_ERR_TIMEOUT))) {
+        ok = false;
+        break;
       }
-      if (!mes::mbar_wait_warp(&full[s], ph, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) { ok = false; break; }
       mes::tc_fence_after();
-      const uint32_t* wsrc = ws + s * (C::kWStage / 4) + half * C::kWords * kBN + row;
-      uint32_t a[4 * C::kWords];
+      const uint8_t* w = wst + s * C::kWStage;
+      const GroupParams gp =
+          make_group(reinterpret_cast<const uint32_t*>(w + C::kWBytes + 256)[row >> 3], zshift,
+                     reinterpret_cast<const uint16_t*>(w + C::kWBytes)[row]);
+      const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(w) + half * C::kWords * kBN + row;
+      uint32_t av[4 * C::kWords];
 #pragma unroll
-      for (int i = 0; i < C::kWords; ++i) {
-        const uint32_t w = wsrc[i * kBN];
-        a[4 * i + 0] = dq_pair(w, gp);
-        a[4 * i + 1] = dq_pair(w >> 4, gp);
-        a[4 * i + 2] = dq_pair(w >> 8, gp);
-        a[4 * i + 3] = dq_pair(w >> 12, gp);
+      for (int j = 0; j < C::kWords; ++j) {
+        const uint32_t wv = wsrc[j * kBN];
+        av[4 * j + 0] = dq_pair(wv, gp);
+        av[4 * j + 1] = dq_pair(wv >> 4, gp);
+        av[4 * j + 2] = dq_pair(wv >> 8, gp);
+        av[4 * j + 3] = dq_pair(wv >> 12, gp);
       }
-      if constexpr (C::kWords == 8) mes::tmem_st32(tmem_a + s * 32 + lane_off, a);
-      else mes::tmem_st16(tmem_a + s * 32 + half * 16 + lane_off, a);
+      if constexpr (C::kWords == 8) mes::tmem_st32(tmem_a + a * 32 + lane_off, av);
+      else mes::tmem_st16(tmem_a + a * 32 + half * 16 + lane_off, av);
       mes::tmem_wait_st();
       mes::tc_fence_before();
       __syncwarp();
-      if (lane == 0) mes::mbar_arrive(&afull[s]);
+      if (lane == 0) mes::mbar_arrive(&afull[a]);
       __syncwarp();
     }
-    if (ok && mes::mbar_wait_warp(accum, 0, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
-      mes::tc_fence_after();
-      const float b = bias ? __bfloat162float(bias[n]) : 0.f;
-      __nv_bfloat16* buf = outbuf + (warp - 2) * (C::kOutBuf / 2);
-      bool stored = false;
+    epi_ok = ok && mes::mbar_wait_warp(accum, 0, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT);
+    if (epi_ok) mes::tc_fence_after();
+    if (epi_ok && split == 1) {
 #pragma unroll 1
       for (int c0 = half * C::kChunk; c0 < BT; c0 += C::kHalves * C::kChunk) {
-        uint32_t v[C::kChunk];
-        if constexpr (C::kChunk == 32) mes::tmem_ld32(tmem + lane_off + c0, v);
-        else mes::tmem_ld16(tmem + lane_off + c0, v);
-        mes::tmem_wait_ld();
         if (t0 + c0 >= M) break;  // rows past the end of X: nothing to store
-        if constexpr (C::kSilu) {
-          silu_chunk<C::kChunk>(v, lane, buf, stored, &map_y, n0 / 2 + q * 16, t0 + c0);
-        } else if constexpr (C::kResidual) {
-          // Each lane owns feature n; a warp touches 32 consecutive fp32 per token row.
-          const int rows = min(C::kChunk, M - (t0 + c0));
-          float* rp = R + (int64_t)(t0 + c0) * ldr + n;
-          float rv[C::kChunk];
-#pragma unroll
-          for (int j = 0; j < C::kChunk; ++j) rv[j] = j < rows ? rp[(int64_t)j * ldr] : 0.f;
-#pragma unroll
-          for (int j = 0; j < C::kChunk; ++j)
-            if (j < rows) rp[(int64_t)j * ldr] = rv[j] + (__uint_as_float(v[j]) + b);
-        } else {
-          if (stored) {  // the previous TMA store must have read the staging block
-            if (lane == 0) mes::tma_store_wait_read<0>();
-            __syncwarp();
-          }
-#pragma unroll
-          for (int j = 0; j < C::kChunk; ++j)
-            buf[j * 32 + lane] = __float2bfloat16_rn(__uint_as_float(v[j]) + b);
-          mes::fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            mes::tma_store_2d(&map_y, buf, n0 + q * 32, t0 + c0);
-            mes::tma_store_commit();
-          }
-          __syncwarp();
-          stored = true;
-        }
-      }
-      if (!C::kResidual) {
-        if (lane == 0) mes::tma_store_wait_all<0>();
-        __syncwarp();
+        uint32_t v[C::kChunk];
+        load_acc(v, c0);
+        store_chunk(v, c0);
       }
     }
+  }
+
+  if (split > 1) {
+    // ------------------------------ split-K reduction ---------------------------------
+    // Partial tile layout: token j, feature f at float index ((j / 4) * 128 + f) * 4 + j % 4,
+    // so one lane's four consecutive tokens are one 16-byte word and a warp's 32 features
+    // are 512 contiguous bytes.
+    const int half = warp >= 2 ? (warp - 2) / 4 : 0;
+    if (warp >= 2 && epi_ok) {
+      mes::fence_proxy_async_smem();  // the ring was last written by TMA
+#pragma unroll 1
+      for (int c0 = half * C::kChunk; c0 < BT; c0 += C::kHalves * C::kChunk) {
+        if (t0 + c0 >= M) break;
+        uint32_t v[C::kChunk];
+        load_acc(v, c0);
+#pragma unroll
+        for (int j = 0; j < C::kChunk; j += 4)
+          *reinterpret_cast<float4*>(red + (((c0 + j) / 4) * kBN + row) * 4) =
+              make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                          __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+      }
+    }
+    mes::cluster_sync();
+    if (warp >= 2 && epi_ok) {
+      const uint32_t red_addr = mes::smem_u32(red);
+#pragma unroll 1
+      for (int c0 = half * C::kChunk; c0 < BT; c0 += C::kHalves * C::kChunk) {
+        if (t0 + c0 >= M) break;
+        if (((c0 / C::kChunk) * 4 + q) % split != rank) continue;
+        float acc[C::kChunk];
+#pragma unroll 1
+        for (int p = 0; p < split; ++p) {
+          const uint32_t base = mes::mapa_shared(red_addr, (uint32_t)p);
+#pragma unroll
+          for (int j = 0; j < C::kChunk; j += 4) {
+            const float4 f = mes::ld_dsmem_f4(base + (uint32_t)((((c0 + j) / 4) * kBN + row) * 16));
+            if (p == 0) {
+              acc[j] = f.x; acc[j + 1] = f.y; acc[j + 2] = f.z; acc[j + 3] = f.w;
+            } else {
+              acc[j] += f.x; acc[j + 1] += f.y; acc[j + 2] += f.z; acc[j + 3] += f.w;
+            }
+          }
+        }
+        uint32_t v[C::kChunk];
+#pragma unroll
+        for (int j = 0; j < C::kChunk; ++j) v[j] = __float_as_uint(acc[j]);
+        store_chunk(v, c0);
+      }
+    }
+    mes::cluster_sync();  // peers' partial tiles stay alive until every read is done
+  }
+  if (warp >= 2 && !C::kResidual) {
+    if (lane == 0) mes::tma_store_wait_all<0>();
+    __syncwarp();
   }
 
   mes::tc_fence_before();
@@ -1051,29 +1151,99 @@ inline bool make_out_map(CUtensorMap* my, const CUtensorMap& fallback, int epi, 
                                epi == kEpiSilu ? 16 : 32, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-template <int BT, int STAGES, int EPI, int NDQ>
+// Number of CTAs that share the K range of one tile (small-M kernel): enough for one CTA
+// per SM outside the reserve, at most 8 (a portable cluster) and at most the K / 128 weight
+// groups; reduced until the clusters of one wave fit on the device at once.  The
+// environment variable MES_GEMM_SPLIT (read once) fixes it for tuning; 0 or unset = auto.
+// `clusters_by` caches the resident-cluster count per device and split size for `kern`.
+template <typename Kern>
+int choose_split(Kern kern, cudaLaunchConfig_t cfg, int64_t tiles, int64_t groups,
+                 std::atomic<int> (&clusters_by)[64][9]) {
+  static const int forced = [] {
+    const char* v = getenv("MES_GEMM_SPLIT");
+    const int c = v ? atoi(v) : 0;
+    return (c < 0 || c > 8) ? 0 : c;
+  }();
+  const int sms = mes_host::persistent_ctas();
+  int split = forced > 0 ? forced : (tiles >= sms ? 1 : (int)(sms / tiles));
+  if (split > 8) split = 8;
+  if (split > groups) split = (int)groups;
+  if (forced > 0 || split <= 1) return split < 1 ? 1 : split;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 1;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  for (; split > 1; --split) {
+    int clusters = clusters_by[dev & 63][split].load(std::memory_order_relaxed);
+    if (clusters == 0) {
+      attr[0].val.clusterDim.x = split;
+      cfg.gridDim = dim3((unsigned)split, 1, 1);
+      if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        clusters = 0;
+      }
+      if (clusters <= 0) clusters = -1;
+      clusters_by[dev & 63][split].store(clusters, std::memory_order_relaxed);
+    }
+    if (clusters >= tiles) break;
+  }
+  return split;
+}
+
+// One-tile-per-CTA launch (split-K over clusters when the tile grid leaves SMs idle).
+template <int BT, int STAGES, int ASLOTS, int EPI, int NDQ>
 int launch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
                 const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
                 int64_t N, int64_t K, cudaStream_t stream) {
-  using C = Cfg<BT, STAGES, EPI, NDQ>;
+  using C = Cfg<BT, STAGES, ASLOTS, EPI, NDQ>;
+  auto kern = awq_gemm_kernel<BT, STAGES, ASLOTS, EPI, NDQ>;
   static std::atomic<uint64_t> attr_done{0};
-  const int st = mes_host::once_per_device(attr_done, [] {
-    return cudaFuncSetAttribute(awq_gemm_kernel<BT, STAGES, EPI, NDQ>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) == cudaSuccess
-               ? MES_OK : MES_ERR_CUDA;
+  const int st = mes_host::once_per_device(attr_done, [&] {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemLaunch) !=
+        cudaSuccess)
+      return MES_ERR_CUDA;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, C::kThreads, C::kSmemLaunch) !=
+            cudaSuccess ||
+        per_sm < 1 || per_sm > C::kCtasByTmem)
+      return MES_ERR_CUDA;  // more CTAs per SM than TMEM serves: refuse rather than risk a wait
+    return MES_OK;
   });
   if (st != MES_OK) return st;
-  CUtensorMap mx, mw, my;
+  CUtensorMap mx, mw, ms, mz, my;
   if (!mes_host::make_map_2d(&mx, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, ldx, BT, kBK,
                              CU_TENSOR_MAP_SWIZZLE_128B) ||
       !mes_host::make_map_2d(&mw, qw, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, K / 8, N, N, kBK / 8, kBN,
-                             CU_TENSOR_MAP_SWIZZLE_NONE))
+                             CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !mes_host::make_map_2d(&ms, scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, K / kGroup, N, N, 1,
+                             kBN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !mes_host::make_map_2d(&mz, qzeros, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, K / kGroup, N / 8,
+                             N / 8, 1, kBN / 8, CU_TENSOR_MAP_SWIZZLE_NONE))
     return MES_ERR_INVALID;
   if (!make_out_map(&my, mx, EPI, Y, M, N, ldy, C::kChunk)) return MES_ERR_INVALID;
-  dim3 grid((unsigned)(N / kBN), (unsigned)((M + BT - 1) / BT));
-  awq_gemm_kernel<BT, STAGES, EPI, NDQ><<<grid, C::kThreads, C::kSmem, stream>>>(
-      mx, mw, my, qzeros, (const uint16_t*)scales, (const __nv_bfloat16*)bias,
-      C::kResidual ? (float*)Y : nullptr, ldy, (int)M, (int)N, (int)K);
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(C::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmemLaunch;
+  cfg.stream = stream;
+  const int64_t tiles = (N / kBN) * ((M + BT - 1) / BT);
+  static std::atomic<int> clusters_by[64][9];  // resident clusters, per device and split
+  const int split = choose_split(kern, cfg, tiles, K / kGroup, clusters_by);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = split;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = split > 1 ? 1 : 0;
+  cfg.gridDim = dim3((unsigned)(N / kBN * split), (unsigned)((M + BT - 1) / BT), 1);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mx, mw, ms, mz, my, (const __nv_bfloat16*)bias,
+                                           C::kResidual ? (float*)Y : nullptr, ldy, (int)M, (int)N,
+                                           (int)K, split);
+  if (e != cudaSuccess) return MES_ERR_CUDA;
   return mes_host::from_cuda(cudaGetLastError());
 }
 
@@ -1172,7 +1342,8 @@ int launch_gemm_pair(const void* X, int64_t ldx, const int32_t* qw, const int32_
 //     epilogues on single CTAs (measured at M = 20000: residual N = 1024, K = 2048 865 vs
 //     788 TFLOP/s; bf16 N = 6144, K = 1024 1138 vs 1170; SiLU 1117 vs 1159);
 //   1 persistent single CTA, 192 tokens, dequantised A in TMEM;
-//   2 one 256-token tile per CTA;
+//   2 one 256-token tile per CTA (the default too while the 256-token tiles number at most
+//     half the SMs; K is then split over clusters);
 //   3 persistent single CTA, 256 tokens, dequantised A in shared memory;
 //   4 CTA pairs wherever N is a multiple of 256.
 // Narrower single-CTA tiles do not pay: a tile's time is set by its 128 x K weights far
@@ -1192,12 +1363,17 @@ template <int EPI>
 int dispatch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
                   const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
                   int64_t N, int64_t K, cudaStream_t s) {
-  if (M <= 16) return launch_gemm<16, 6, EPI, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-  if (M <= 32) return launch_gemm<32, 6, EPI, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-  if (M <= 64) return launch_gemm<64, 6, EPI, 4>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-  switch (large_m_config()) {
+  if (M <= 16) return launch_gemm<16, 16, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  if (M <= 32) return launch_gemm<32, 11, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  if (M <= 64) return launch_gemm<64, 7, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  const int config = large_m_config();
+  // Fewer 256-token tiles than half the SMs: one tile per CTA with K split over clusters
+  // keeps the SMs busy that a persistent kernel would leave idle.
+  const int64_t tiles256 = (N / kBN) * ((M + 255) / 256);
+  if (config == 2 || (config != 1 && 2 * tiles256 <= mes_host::persistent_ctas()))
+    return launch_gemm<256, 5, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  switch (config) {
     case 1: return launch_gemm_persistent<192, 4, 4, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
-    case 2: return launch_gemm<256, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
     case 3: return launch_gemm_persistent<256, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
     case 4:
       if (N % (2 * kBN) == 0) return launch_gemm_pair<EPI>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);

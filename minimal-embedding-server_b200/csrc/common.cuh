@@ -92,13 +92,14 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
   return __all_sync(0xffffffffu, ok);
 }
 
-// ------------------------------- CTA pairs (clusters of 2) ------------------------------
+// ----------------------------- clusters (CTA pairs, split-K) ----------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-// Every thread of both CTAs arrives, then waits for all of them (release / acquire).
+// Every thread of every CTA of the cluster arrives, then waits for all of them
+// (release / acquire).
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
@@ -116,6 +117,15 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t cta_addr, uint32_t rank
 // arrival here.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// 16-byte load from the shared memory of any CTA of the cluster (address from mapa_shared).
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
 }
 
 // ------------------------------------- TMA ----------------------------------------------

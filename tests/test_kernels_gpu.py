@@ -317,3 +317,64 @@ def test_awq_gemm_tile_variants(config):
     r = subprocess.run([sys.executable, "-c", _VARIANT_CHECK, root], env=env,
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-3000:]
+
+
+# ---------------------------------------------------------------- split-K over clusters
+_SPLIT_CHECK = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+import __graft_entry__; __graft_entry__.load_package()
+from mes_b200 import _C
+from oracle import awq as oawq
+# Shapes of the one-tile-per-CTA kernel (M <= 64, or few 256-token tiles): 16/32/64/256-
+# token tiles, ragged last tiles, K of 5 and 7 groups (uneven shares), bias, and all three
+# epilogues.  Every result is computed twice and must repeat bit for bit.
+for M, K, N, kind, bias in [(1, 640, 128, "bf16", True), (16, 896, 256, "res", False),
+                            (33, 1024, 384, "silu", False), (64, 640, 256, "bf16", False),
+                            (100, 896, 256, "res", True), (300, 1024, 512, "silu", False),
+                            (256, 2048, 128, "bf16", True)]:
+    qw, qz, sc = oawq.random_awq(K, N, seed=M + K)
+    g = torch.Generator().manual_seed(M)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    b = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16) if bias else None
+    w = torch.from_numpy(oawq.bf16_bits_to_f32(oawq.dequant_bf16_bits(qw, qz, sc)))
+    acc = x.float() @ w + (b.float() if b is not None else 0)
+    dq, ds = torch.from_numpy(qz).cuda(), torch.from_numpy(sc).view(torch.int16).cuda()
+    bd = None if b is None else b.cuda()
+    outs = []
+    for _ in range(2):
+        if kind == "silu":
+            qwi, qzi, sci = _C.interleave_gate_up(torch.from_numpy(qw).cuda(), dq, ds)
+            got = _C.awq_gemm_silu(x.cuda(), _C.awq_repack(qwi), qzi, sci).float().cpu()
+            ref = torch.nn.functional.silu(acc[:, : N // 2]) * acc[:, N // 2:]
+            tol = 1e-2 * ref.abs().max().item() + 1e-3
+        elif kind == "res":
+            r0 = torch.randn(M, N, generator=torch.Generator().manual_seed(K))
+            r = r0.cuda()
+            _C.awq_gemm_residual(x.cuda(), _C.awq_repack(torch.from_numpy(qw).cuda()), dq, ds, r, bd)
+            got, ref = r.cpu(), r0 + acc
+            tol = 1e-4 * ref.abs().max().item() + 1e-4
+        else:
+            got = _C.awq_gemm(x.cuda(), _C.awq_repack(torch.from_numpy(qw).cuda()), dq, ds, bd).float().cpu()
+            ref, tol = acc, 1e-2 * acc.abs().max().item() + 1e-3
+        err = (got - ref).abs().max().item()
+        assert err <= tol, (M, K, N, kind, err, tol)
+        outs.append(got)
+    assert torch.equal(outs[0], outs[1]), ("not deterministic", M, K, N, kind)
+assert _C.take_device_error() == 0
+print("ok")
+"""
+
+
+@pytest.mark.parametrize("split", ["1", "2", "3", "5", "8"])
+def test_awq_gemm_split_k(split):
+    # K split over clusters of `split` CTAs (MES_GEMM_SPLIT, read once per process, so each
+    # value runs in a child process; capped by the K / 128 groups of the shape).  Same
+    # tolerances as the unsplit tests; the cluster reduction adds the partial tiles in rank
+    # order, so repeated calls agree bit for bit.
+    import os, subprocess, sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, MES_GEMM_SPLIT=split)
+    r = subprocess.run([sys.executable, "-c", _SPLIT_CHECK, root], env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-3000:]
