@@ -54,6 +54,10 @@ def parse_args():
     ap.add_argument("--impl", choices=["mes", "reference"], default="mes")
     ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "ew"], default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemm-shapes", default="qkv,o,gate_up,down",
+                    help="c3 only: comma list of projection shapes to time")
+    ap.add_argument("--gemm-m", default="16,256,2048,20000,120000",
+                    help="c3 only: comma list of token counts M")
     return ap.parse_args()
 
 
@@ -416,10 +420,11 @@ def run_gemm_micro(args):
     peak_burst, _, hbm, peak_kind = peaks()
     shapes = {"qkv": (2560, 6144), "o": (4096, 2560), "gate_up": (2560, 19456), "down": (9728, 2560)}
     gen = torch.Generator(device=dev).manual_seed(0)
-    for name, (K, N) in shapes.items():
+    for name in args.gemm_shapes.split(","):
+        K, N = shapes[name]
         qw, qz, sc = synthetic.random_awq(K, N, gen, dev)
         qwm, sc16 = _C.awq_repack(qw), sc.view(torch.int16)
-        for M in (16, 256, 2048, 20000, 120000):
+        for M in (int(m) for m in args.gemm_m.split(",")):
             x = torch.randn(M, K, generator=gen, device=dev).to(torch.bfloat16)
             y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
             t = cold_launch_time(lambda: _C.awq_gemm(x, qwm, qz, sc16, None, y), args, dev)
