@@ -122,12 +122,15 @@ __global__ void rmsnorm_kernel(const XT* x, const RT* residual, const uint4* __r
 }
 
 // ------------------------------ q/k RMSNorm + NeoX RoPE --------------------------------
-// 16 threads per (token, group of kGroupHeads heads): thread j owns elements 8j..8j+7 of
-// each 128-wide head, so the token's cos/sin values and the norm weights are loaded once
-// per group and the group's head loads are all in flight together (kGroupHeads x 16 bytes
-// per thread).  Units are token-major, so a block covers consecutive kilobytes of the
-// packed qkv rows.  The rotate-half partner of thread j is j ^ 8.
+// 8 threads per (token, group of kGroupHeads heads): thread j owns elements 8j..8j+7 and
+// 64+8j..64+8j+7 of each 128-wide head, so both elements that the NeoX rotate-half pairs are
+// in the same thread (the rotation needs no shuffle) and a head's sum of squares takes three
+// shuffles.  The token's cos/sin values (one set serves both halves) and the norm weights are
+// loaded once per group, and the group's head loads are all in flight together
+// (2 x kGroupHeads x 16 bytes per thread).  Units are token-major, so a block covers
+// consecutive kilobytes of the packed qkv rows.
 constexpr int kGroupHeads = 8;
+constexpr int kRopeThreads = 8;  // threads per unit
 template <bool kF32Cache>
 __device__ __forceinline__ void load_cos_sin(const void* cos_sin, int64_t ps, int cj, float (&c)[8],
                                              float (&s)[8]) {
@@ -145,60 +148,81 @@ __device__ __forceinline__ void load_cos_sin(const void* cos_sin, int64_t ps, in
 }
 
 template <bool kNorm, bool kF32Cache>
-__global__ void __launch_bounds__(256, 3)
+__global__ void __launch_bounds__(256, 2)
 qknorm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, const int64_t* __restrict__ pos,
                    const void* __restrict__ cos_sin, int64_t max_pos, const uint4* __restrict__ qw,
                    const uint4* __restrict__ kw, int T, int Hq, int Hkv, float eps) {
   const int nh = Hq + Hkv;
   const int ngroups = (nh + kGroupHeads - 1) / kGroupHeads;
-  const int unit = blockIdx.x * 16 + (threadIdx.x >> 4);
-  const int j = threadIdx.x & 15;
+  const int unit = blockIdx.x * (256 / kRopeThreads) + (threadIdx.x / kRopeThreads);
+  const int j = threadIdx.x % kRopeThreads;
   const bool valid = unit < T * ngroups;
   const int t = valid ? unit / ngroups : 0;
   const int h0 = (unit - t * ngroups) * kGroupHeads;
   uint4* row = reinterpret_cast<uint4*>(qkv + (int64_t)t * ld) + h0 * 16 + j;
-  uint4 raw[kGroupHeads];
+  uint4 lo[kGroupHeads], hi[kGroupHeads];
 #pragma unroll
-  for (int u = 0; u < kGroupHeads; ++u)
-    raw[u] = (valid && h0 + u < nh) ? row[u * 16] : make_uint4(0, 0, 0, 0);
+  for (int u = 0; u < kGroupHeads; ++u) {
+    const bool live = valid && h0 + u < nh;
+    lo[u] = live ? row[u * 16] : make_uint4(0, 0, 0, 0);
+    hi[u] = live ? row[u * 16 + 8] : make_uint4(0, 0, 0, 0);
+  }
   int64_t ps = valid ? __ldg(pos + t) : 0;
   if (ps < 0 || ps >= max_pos) {
     if (valid && j == 0 && h0 == 0) atomicCAS(&g_err_elementwise, 0, MES_ERR_INVALID);
     ps = 0;
   }
   float c[8], s[8];
-  load_cos_sin<kF32Cache>(cos_sin, ps, (j & 7) * 8, c, s);
-  uint4 wq = make_uint4(0, 0, 0, 0), wk = make_uint4(0, 0, 0, 0);  // unpacked per head
+  load_cos_sin<kF32Cache>(cos_sin, ps, j * 8, c, s);
+  // Norm weights of this thread's two 8-element slices, for q heads and for k heads.
+  uint4 wq_lo = make_uint4(0, 0, 0, 0), wq_hi = wq_lo, wk_lo = wq_lo, wk_hi = wq_lo;
   if (kNorm) {
-    if (h0 < Hq) wq = __ldg(qw + j);
-    if (Hkv > 0 && h0 + kGroupHeads > Hq) wk = __ldg(kw + j);
+    if (h0 < Hq) {
+      wq_lo = __ldg(qw + j);
+      wq_hi = __ldg(qw + 8 + j);
+    }
+    if (Hkv > 0 && h0 + kGroupHeads > Hq) {
+      wk_lo = __ldg(kw + j);
+      wk_hi = __ldg(kw + 8 + j);
+    }
   }
 #pragma unroll
   for (int u = 0; u < kGroupHeads; ++u) {
-    // Every lane runs all the group's heads (the two units of a warp may differ in head
-    // count and the shuffles use the full mask); heads past the end compute on zeros and
-    // store nothing.
-    float f[8];
-    unpack8(raw[u], f);
+    // Every lane runs all the group's heads (the units of a warp may differ in head count
+    // and the shuffles use the full mask); heads past the end compute on zeros and store
+    // nothing.
+    float a[8], b[8];
+    unpack8(lo[u], a);
+    unpack8(hi[u], b);
     if (kNorm) {
       float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+      for (int i = 0; i < 8; ++i) ss += a[i] * a[i];
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      for (int i = 0; i < 8; ++i) ss += b[i] * b[i];
+#pragma unroll
+      for (int o = kRopeThreads / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       const float rs = rsqrtf(ss * (1.0f / 128.0f) + eps);
-      float wf[8];
-      unpack8(h0 + u < Hq ? wq : wk, wf);
+      const bool is_q = h0 + u < Hq;
+      float wa[8], wb[8];
+      unpack8(is_q ? wq_lo : wk_lo, wa);
+      unpack8(is_q ? wq_hi : wk_hi, wb);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) f[i] = round_bf16(round_bf16(f[i] * rs) * wf[i]);
+      for (int i = 0; i < 8; ++i) {
+        a[i] = round_bf16(round_bf16(a[i] * rs) * wa[i]);
+        b[i] = round_bf16(round_bf16(b[i] * rs) * wb[i]);
+      }
     }
-    float o[8];
+    float oa[8], ob[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float p = __shfl_xor_sync(0xffffffffu, f[i], 8);
-      o[i] = j < 8 ? f[i] * c[i] - p * s[i] : f[i] * c[i] + p * s[i];
+      oa[i] = a[i] * c[i] - b[i] * s[i];
+      ob[i] = b[i] * c[i] + a[i] * s[i];
     }
-    if (valid && h0 + u < nh) row[u * 16] = pack8(o);
+    if (valid && h0 + u < nh) {
+      row[u * 16] = pack8(oa);
+      row[u * 16 + 8] = pack8(ob);
+    }
   }
 }
 
@@ -438,8 +462,8 @@ extern "C" int mes_qknorm_rope(void* qkv, int64_t ld, const int64_t* positions,
   if (!aligned16(qkv) || !aligned16(cos_sin) || (apply_norm && (!aligned16(q_w) || !aligned16(k_w))))
     return MES_ERR_ALIGN;
   const int64_t units = T * (((int64_t)Hq + Hkv + kGroupHeads - 1) / kGroupHeads);
-  if (units > 0x7fffffffLL - 16) return MES_ERR_INVALID;
-  const unsigned blocks = (unsigned)((units + 15) / 16);
+  if (units > 0x7fffffffLL - 256) return MES_ERR_INVALID;
+  const unsigned blocks = (unsigned)((units + 256 / kRopeThreads - 1) / (256 / kRopeThreads));
   cudaStream_t s = (cudaStream_t)stream;
   __nv_bfloat16* p = (__nv_bfloat16*)qkv;
   const uint4* qwp = (const uint4*)q_w;
