@@ -319,6 +319,21 @@ def test_awq_gemm_tile_variants(config):
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-3000:]
 
 
+def test_awq_gemm_split_k_under_sm_reserve():
+    # The overlapped tensor-parallel forward keeps SMs free for NCCL (mes_set_sm_reserve); the
+    # split-K launch then sizes its clusters for the remaining SMs.  Same tolerance as
+    # test_awq_gemm_matches_fp32; the reserve is restored whatever happens.
+    try:
+        _C.set_sm_reserve(64)
+        for M, K, N in [(16, 2048, 1024), (200, 1024, 512), (64, 4096, 256)]:
+            y, ref = _gemm_case(M, K, N, M % 2 == 0, seed=M + 7)
+            err = (y - ref).abs().max().item()
+            assert err <= 1e-2 * ref.abs().max().item() + 1e-3, (M, K, N, err)
+    finally:
+        _C.set_sm_reserve(0)
+    assert _C.take_device_error() == 0
+
+
 # ---------------------------------------------------------------- split-K over clusters
 _SPLIT_CHECK = r"""
 import sys, torch
