@@ -1342,8 +1342,8 @@ int launch_gemm_pair(const void* X, int64_t ldx, const int32_t* qw, const int32_
 //     epilogues on single CTAs (measured at M = 20000: residual N = 1024, K = 2048 865 vs
 //     788 TFLOP/s; bf16 N = 6144, K = 1024 1138 vs 1170; SiLU 1117 vs 1159);
 //   1 persistent single CTA, 192 tokens, dequantised A in TMEM;
-//   2 one 256-token tile per CTA (the default too while the 256-token tiles number at most
-//     half the SMs; K is then split over clusters);
+//   2 one 256-token tile per CTA (the default too for M <= 256 while the tiles number at
+//     most half the SMs; K is then split over clusters);
 //   3 persistent single CTA, 256 tokens, dequantised A in shared memory;
 //   4 CTA pairs wherever N is a multiple of 256.
 // Narrower single-CTA tiles do not pay: a tile's time is set by its 128 x K weights far
@@ -1367,10 +1367,11 @@ int dispatch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* 
   if (M <= 32) return launch_gemm<32, 11, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
   if (M <= 64) return launch_gemm<64, 7, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
   const int config = large_m_config();
-  // Fewer 256-token tiles than half the SMs: one tile per CTA with K split over clusters
-  // keeps the SMs busy that a persistent kernel would leave idle.
-  const int64_t tiles256 = (N / kBN) * ((M + 255) / 256);
-  if (config == 2 || (config != 1 && 2 * tiles256 <= mes_host::persistent_ctas()))
+  // One 256-token tile row that covers at most half the SMs: one tile per CTA with K split
+  // over clusters keeps the SMs busy that a persistent kernel would leave idle.  Larger M
+  // stays on the persistent kernels, so every batch of more than 256 tokens accumulates
+  // each output in the same order (a row's result does not depend on the batch around it).
+  if (config == 2 || (config != 1 && M <= 256 && 2 * (N / kBN) <= mes_host::persistent_ctas()))
     return launch_gemm<256, 5, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
   switch (config) {
     case 1: return launch_gemm_persistent<192, 4, 4, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);

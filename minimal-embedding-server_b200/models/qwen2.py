@@ -200,6 +200,10 @@ class DecoderModel(nn.Module):
 
     # Tensor parallelism: below this many tokens the batch is not split for overlap.
     overlap_min_tokens = int(os.environ.get("MES_TP_OVERLAP_MIN_TOKENS", "4096"))
+    # Neither micro-batch may have 256 tokens or fewer: the GEMMs split K over clusters for
+    # such batches, which rounds differently from the whole batch's kernels, and the
+    # overlapped forward must equal the unsplit one bit for bit.
+    overlap_min_part = 257
     @staticmethod
     def overlap_reserved_sms(world_size: int) -> int:
         """SMs kept free of the persistent kernels while all-reduces overlap them: the NCCL
@@ -248,12 +252,14 @@ class DecoderModel(nn.Module):
             return None
         return cls._nearest_middle(np.flatnonzero(pos[1:] != pos[:-1] + 1) + 1, T)
 
-    @staticmethod
-    def _nearest_middle(starts, T: int) -> int | None:
+    @classmethod
+    def _nearest_middle(cls, starts, T: int) -> int | None:
+        import numpy as np
+        starts = np.asarray(starts)
+        starts = starts[(starts >= cls.overlap_min_part) & (T - starts >= cls.overlap_min_part)]
         if len(starts) == 0:
             return None
-        import numpy as np
-        return int(starts[np.argmin(np.abs(np.asarray(starts) - T // 2))])
+        return int(starts[np.argmin(np.abs(starts - T // 2))])
 
     def _forward_overlapped(self, input_ids, positions, split: int) -> torch.Tensor:
         """Tensor-parallel forward as two micro-batches of whole sequences, A = tokens

@@ -113,6 +113,11 @@ def test_overlap_split_is_a_sequence_start_near_the_middle(monkeypatch):
     assert qwen2.DecoderModel.overlap_split_host(pos) == 3000     # starts 1000, 1700, 3000, 4000
     assert qwen2.DecoderModel.overlap_split_host(np.arange(5000)) is None       # one sequence
     assert qwen2.DecoderModel.overlap_split_host(np.arange(100)) is None        # below the threshold
+    # A micro-batch of 256 tokens or fewer is never cut off (its GEMMs would split K).
+    edge = np.concatenate([np.arange(4800), np.arange(200)])
+    assert qwen2.DecoderModel.overlap_split_host(edge) is None
+    edge = np.concatenate([np.arange(200), np.arange(2000), np.arange(2800)])
+    assert qwen2.DecoderModel.overlap_split_host(edge) == 2200
     monkeypatch.setattr(qwen2, "_tp_size", lambda: 1)
     assert qwen2.DecoderModel.overlap_split_host(pos) is None                  # tp == 1
     assert qwen2.DecoderModel.overlap_reserved_sms(2) == 16
