@@ -3,18 +3,22 @@
 //
 // Y[M, N] = X[M, K] * W[K, N] (+ bias), W[k, n] = bf16_rne((q - z) * s).
 //
-// The product is computed transposed, Y^T = W^T X^T, so that the weights are the MMA's
-// A operand and can live in tensor memory:
-//   * a TMA warp streams X tiles (BT tokens x 64 k, bf16, 128-byte swizzle) and the packed
-//     weight tile (8 words x 128 features of the kernel layout) into a ring of smem stages;
-//   * four dequant warps (one per TMEM lane quadrant, one output feature per thread) turn
-//     8 words = 64 k of their feature into 32 bf16x2 registers and write them with
-//     tcgen05.st into the stage's TMEM A slot - the bf16 weights never touch smem or HBM;
-//   * one thread issues tcgen05.mma (M = 128 features, N = BT tokens, K = 16) reading A from
-//     TMEM and B (= X) from smem, accumulating fp32 in TMEM, and frees each stage with
-//     tcgen05.commit;
-//   * the same four warps drain the accumulator (tcgen05.ld), add the bias, convert to bf16
-//     and write 32x32 blocks through smem with TMA stores.
+// The product is computed transposed, Y^T = W^T X^T, so that the dequantised weights are
+// the MMA's A operand (128 features per CTA) and the tokens its N dimension.  Every kernel
+// here has the same roles:
+//   * a TMA warp streams X tiles (BT tokens x 64 k, bf16, 128-byte swizzle), the packed
+//     weight tile (8 words x 128 features of the kernel layout) and the group's scales and
+//     zero words into a ring of shared-memory stages;
+//   * dequant warps (one output feature per thread) turn 8 words = 64 k of their feature
+//     into 32 bf16x2 values and store them as the step's A tile - into TMEM with tcgen05.st
+//     (small-M kernel) or into shared memory with the 128-byte swizzle (persistent and
+//     CTA-pair kernels); the bf16 weights never reach HBM;
+//   * one thread issues tcgen05.mma (M = 128 features, or 256 across a CTA pair; N = BT
+//     tokens; K = 16), accumulating fp32 in TMEM, and frees each stage with tcgen05.commit;
+//   * epilogue warps drain the accumulator (tcgen05.ld) and add the bias, then write bf16
+//     through shared memory with TMA stores, add into an fp32 residual, or apply
+//     SiLU-and-mul.
+// Which kernel runs for which M, N and epilogue is decided in dispatch_gemm.
 //
 // Exact dequantisation in bf16x2 arithmetic: the code pair (q_k, q_k+1) is extracted as the
 // bf16 pair (128 + q) with one LOP3 (the nibble interleave puts k and k+1 at bits 4j and
