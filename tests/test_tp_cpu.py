@@ -118,6 +118,11 @@ def test_overlap_split_is_a_sequence_start_near_the_middle(monkeypatch):
     assert qwen2.DecoderModel.overlap_split_host(edge) is None
     edge = np.concatenate([np.arange(200), np.arange(2000), np.arange(2800)])
     assert qwen2.DecoderModel.overlap_split_host(edge) == 2200
+    # The model's own path (positions as a torch tensor) applies the same rule.
+    import torch
+    D = qwen2.DecoderModel
+    assert D._overlap_split(D, torch.from_numpy(pos)) == 3000
+    assert D._overlap_split(D, torch.from_numpy(np.concatenate([np.arange(4800), np.arange(200)]))) is None
     monkeypatch.setattr(qwen2, "_tp_size", lambda: 1)
     assert qwen2.DecoderModel.overlap_split_host(pos) is None                  # tp == 1
     assert qwen2.DecoderModel.overlap_reserved_sms(2) == 16
