@@ -13,11 +13,12 @@ pooling + L2 normalisation and the host copies for ``e2e``.
   step.
 * ``roofline``: the AWQ GEMM (the dominant kernel), FLOPs of every launch in the timed
   region / CUDA-event time of those launches, against the measured dense bf16 peak.
-* ``cpu_baseline``: the CPU oracle's fp32 forward (a restatement of the reference's torch
-  forward) on a bounded sample of the same workload, on the host's cores.
+* ``cpu_baseline``: the reference's torch forward as the CPU oracle restates it, in bf16 on
+  the workload's dequantised AWQ checkpoint, over a bounded sample of the batch (2 of its
+  sequences through every layer) on all host cores: one warm-up, median of 3.
 
-``--impl reference`` times that CPU forward alone (rank 0; other ranks exit) and prints
-the same metric.  Run multi-GPU as
+``--impl reference`` times that CPU forward alone (rank 0; other ranks exit), one sample
+per step, and prints the same metric.  Run multi-GPU as
 ``python -m torch.distributed.run --nproc-per-node N bench.py --gpus N``.
 """
 from __future__ import annotations
@@ -36,9 +37,9 @@ sys.path.insert(0, ROOT)
 
 METRIC = "embedding tokens/sec (20x1000-tok batch)"
 
-# DRAM bytes (read + write) of one launch, from `ncu --set full` captures of the same
-# command (profiles/awq_gemm_silu_gate_up_20000x6144x1024.md and
-# profiles/awq_gemm_pair_o_proj_20000x1024x2048.md); None where not captured.
+# DRAM bytes (read + write) of one launch of the kernel, from `ncu --set full` captures of
+# the same command on one B200 (layer 0 of the 20 x 1000-token forward); None where not
+# captured.
 MEASURED_TRAFFIC: dict = {
     ("silu", 20000, 6144, 1024): 117.3e6,       # gate_up + SiLU-and-mul, layer 0
     ("residual", 20000, 1024, 2048): 205.7e6,   # o_proj (CTA pairs), layer 0
@@ -141,62 +142,88 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_forward_tokens_per_s(cfg, sample_tokens: int, layers: int, threads: int,
-                             repeats: int = 1):
-    """The oracle's fp32 forward (dense weights of the same shapes) on `sample_tokens`
-    tokens through `layers` layers; returns tokens/s scaled to the full depth."""
-    import torch
-    from mes_b200 import synthetic
-    from oracle import model as omodel
-    torch.set_num_threads(threads)
-    w = synthetic.dense_weights(cfg, seed=0, num_layers=layers)
-    ids, pos, _ = synthetic.packed_batch([sample_tokens], cfg.vocab_size, seed=1)
-    ids, pos = torch.from_numpy(ids), torch.from_numpy(pos)
-    times = []
-    for _ in range(repeats):
-        t0 = time.perf_counter()
-        omodel.forward(cfg, w, ids, pos, qk_norm=not synthetic.is_qwen2(cfg), num_layers=layers)
-        times.append(time.perf_counter() - t0)
-    per_step = statistics.median(times) * cfg.num_hidden_layers / layers
-    return sample_tokens / per_step, per_step
+CPU_SAMPLE_SEQS = 2   # sequences of the workload's batch in one CPU sample
+
+
+class CpuReferenceSample:
+    """The reference's torch forward, restated by the CPU oracle (``oracle/model.py``,
+    following ``models/qwen3.py`` / ``qwen2.py`` line by line), on a bounded sample of the
+    workload: the first ``CPU_SAMPLE_SEQS`` sequences of the batch through every layer, in
+    bf16 (the reference's deployment dtype), with the workload's seeded AWQ checkpoint
+    dequantised exactly to dense weights (what the reference runs for a dequantised
+    checkpoint; it has no AWQ path).  One ``step()`` is one such forward."""
+
+    def __init__(self, cfg, lengths, threads: int):
+        import torch
+        from mes_b200 import synthetic
+        from oracle import model as omodel
+        torch.set_num_threads(threads)
+        self.cfg, self.threads, self.omodel = cfg, threads, omodel
+        self.lengths = list(lengths[:CPU_SAMPLE_SEQS])
+        dense = omodel.awq_dense_weights(synthetic.awq_weights(cfg, seed=0, device="cpu"))
+        self.weights = {k: v.to(torch.bfloat16) for k, v in dense.items()}
+        del dense
+        ids, pos, last = synthetic.packed_batch(self.lengths, cfg.vocab_size, seed=1)
+        self.ids, self.pos, self.last = (torch.from_numpy(a) for a in (ids, pos, last))
+        self.qk_norm = not synthetic.is_qwen2(cfg)
+        self.tokens = int(sum(self.lengths))
+
+    def step(self):
+        import torch
+        return self.omodel.embed(self.cfg, self.weights, self.ids, self.pos, self.last,
+                                 qk_norm=self.qk_norm, dtype=torch.bfloat16)
+
+    def describe(self) -> str:
+        return (f"{len(self.lengths)} of the batch's sequences ({self.tokens} tokens) through "
+                f"all {self.cfg.num_hidden_layers} layers per step, bf16, the workload's AWQ "
+                f"checkpoint dequantised to dense weights, torch on {self.threads} host threads")
+
+    def timed(self, warmup: int, repeats: int):
+        """Median wall time (s) of `repeats` forwards after `warmup` untimed ones."""
+        for _ in range(warmup):
+            self.step()
+        times = []
+        for _ in range(repeats):
+            t0 = time.perf_counter()
+            self.step()
+            times.append(time.perf_counter() - t0)
+        return statistics.median(times), times
+
+
+def cpu_baseline_entry(cfg, lengths, threads: int) -> dict:
+    """``cpu_baseline`` of the GPU line: one warm-up, then the median of 3 forwards of the
+    CPU sample (the same measurement as ``--impl reference``)."""
+    sample = CpuReferenceSample(cfg, lengths, threads)
+    med, times = sample.timed(warmup=1, repeats=3)
+    return {"value": sample.tokens / med, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": sample.describe() + "; 1 warm-up, median of 3",
+            "seconds_per_sample": times}
 
 
 # ---------------------------------------------------------------------------- reference arm
 def run_reference(args):
+    """The reference arm: the CPU forward of ``CpuReferenceSample`` on all host threads,
+    one sample per step (W untimed, K timed, each timed separately; value = tokens of a
+    sample / median step time).  Rank 0 only; other ranks exit without work."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     cfg, lengths, desc = workload(args.workload)
     threads = os.cpu_count() or 1
-    # Bounded per-step sample: one 1000-token sequence through a subset of the layers,
-    # scaled to the full depth, so that warmup + steps finish in a few minutes.
+    sample = CpuReferenceSample(cfg, lengths, threads)
     steps = max(args.steps, 1)
-    layers = max(1, min(cfg.num_hidden_layers, int(28 * 8 / (steps + args.warmup))))
-    import torch
-    from mes_b200 import synthetic
-    from oracle import model as omodel
-    torch.set_num_threads(threads)
-    w = synthetic.dense_weights(cfg, seed=0, num_layers=layers)
-    ids, pos, _ = synthetic.packed_batch([1000], cfg.vocab_size, seed=1)
-    ids, pos = torch.from_numpy(ids), torch.from_numpy(pos)
-    qk = not synthetic.is_qwen2(cfg)
-    for _ in range(args.warmup):
-        omodel.forward(cfg, w, ids, pos, qk_norm=qk, num_layers=layers)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        omodel.forward(cfg, w, ids, pos, qk_norm=qk, num_layers=layers)
-    dt = (time.perf_counter() - t0) / steps * cfg.num_hidden_layers / layers
-    value = 1000 / dt
-    sample = (f"1 x 1000 tokens through {layers} of {cfg.num_hidden_layers} layers per step, "
-              f"fp32, time scaled to full depth")
+    med, times = sample.timed(warmup=args.warmup, repeats=steps)
+    value = sample.tokens / med
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
-        "ms_per_step": dt * 1000 * sum(lengths) / 1000, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": desc, "tokens": sum(lengths), "sequences": len(lengths)},
+        "ms_per_step": med * 1000, "ms_per_step_is": "median wall time of one timed sample",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded AWQ checkpoint, dequantised; seeded token ids)",
+        "config": {"workload": desc, "tokens": sum(lengths), "sequences": len(lengths),
+                   "sample_tokens": sample.tokens, "sample_sequences": len(sample.lengths)},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "sample": sample.describe()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -262,8 +289,8 @@ def run_mes(args):
             d[2] += f
         return by_shape
 
-    from mes_b200.models.qwen2 import DecoderModel
-    split = DecoderModel.overlap_split_host(pos)
+    layout = worker.layout(pos, exact=True)   # the batch's own layout: no padding
+    split = layout.split
 
     with torch.no_grad():
         # Eager warm-up; the last step records CUDA events around every GEMM: the dominant
@@ -286,7 +313,7 @@ def run_mes(args):
         # captured with it, so every replay times those launches on their stream.
         _C.gemm_events, _C.gemm_event_kinds = [], {probe_key[0]}
         launches0 = _C.launch_count
-        graph, ids_s, pos_s, _ = worker.capture(T, split, ids, pos)
+        graph, ids_s, pos_s, _ = worker.capture(layout, ids, pos)
         launches = (_C.launch_count - launches0) // 2   # capture() runs the forward twice
         captured = _C.gemm_events[len(_C.gemm_events) // 2:]
         _C.gemm_events, _C.gemm_event_kinds = None, None
@@ -322,6 +349,11 @@ def run_mes(args):
         barrier()
         e2e_dt = max_over_ranks(max(e0.elapsed_time(e1) / 1000.0, time.perf_counter() - t0))
 
+        # ---- e2e over a stream of batches of varying size (the server's case) ---------
+        varying = None
+        if args.workload == "c2":
+            varying = run_varying_stream(worker, cfg, barrier, max_over_ranks)
+
     err = _C.take_device_error()
     if err:
         raise RuntimeError(f"device error {err} during the benchmark")
@@ -336,11 +368,7 @@ def run_mes(args):
         value = T * args.steps / dt
         cpu = None
         if not args.no_cpu_baseline and world == 1:
-            threads = os.cpu_count() or 1
-            tps, per = cpu_forward_tokens_per_s(cfg, 1000, 4, threads, repeats=1)
-            cpu = {"value": tps, "unit": UNIT, "cores": threads, "kind": "port",
-                   "sample": "1 x 1000 tokens through 4 of the layers in fp32 (CPU oracle, "
-                             "dense weights of the same shapes), time scaled to full depth"}
+            cpu = cpu_baseline_entry(cfg, lengths, os.cpu_count() or 1)
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
@@ -353,6 +381,7 @@ def run_mes(args):
             "e2e": {"value": T * args.steps / e2e_dt, "unit": UNIT,
                     "h2d_bytes_per_step": int(ids.nbytes + pos.nbytes + last.nbytes),
                     "d2h_bytes_per_step": int(out.numel() * 4)},
+            "e2e_varying": varying,
             "gpu_launches": launches * args.steps,
             "cuda_graph": True,
             "roofline": {"kernel": f"awq_gemm ({kind} epilogue) M={gm} N={gn} K={gk}",
@@ -369,12 +398,45 @@ def run_mes(args):
         }
         print(json.dumps(result), flush=True)
     # CUDA graphs that hold NCCL work are released before the process group goes.
-    worker._graphs.clear()
+    worker.release_graphs()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+def run_varying_stream(worker, cfg, barrier, max_over_ranks, n_batches: int = 16):
+    """``GPUWorker.embed`` over a seeded stream of batches of 20 sequences with lengths
+    uniform in [500, 1500] (10-30 k tokens per batch, a different total each time), as the
+    engine's batcher produces them.  The first pass includes the CUDA-graph captures of the
+    token buckets it meets; the second pass replays them (steady state).  Wall time, max
+    over ranks; tokens/s counts real tokens only."""
+    import time as _time
+    from mes_b200 import synthetic
+    batches = []
+    for i in range(n_batches):
+        lens = synthetic.lengths_uniform(20, 500, 1500, seed=100 + i)
+        batches.append(synthetic.packed_batch(lens, cfg.vocab_size, seed=200 + i))
+    tokens = sum(len(b[0]) for b in batches)
+    out = {}
+    for name in ("first_pass", "steady"):
+        c0 = worker.captures
+        barrier()
+        t0 = _time.perf_counter()
+        for ids, pos, last in batches:
+            worker.embed(ids, pos, last)
+        barrier()
+        dt = max_over_ranks(_time.perf_counter() - t0)
+        out[name] = {"value": tokens / dt, "captures": worker.captures - c0}
+    return {"value": out["steady"]["value"], "unit": UNIT, "batches": n_batches,
+            "tokens": tokens, "tokens_per_batch": [min(len(b[0]) for b in batches),
+                                                   max(len(b[0]) for b in batches)],
+            "first_pass_value": out["first_pass"]["value"],
+            "first_pass_captures": out["first_pass"]["captures"],
+            "steady_captures": out["steady"]["captures"],
+            "how": "GPUWorker.embed per batch (host ids/positions in, fp32 embeddings out), "
+                   "graphs keyed on token buckets"}
 
 
 COLD_L2 = ("before each launch 256 MB written, then another 256 MB read (L2 cold and clean); "

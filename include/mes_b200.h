@@ -44,6 +44,14 @@ const char* mes_status_string(int status);
  * library on the current device (0 if none).  Synchronises the current device. */
 int mes_take_device_error(int* code);
 
+/* Self-test of the bounded device wait that every pipeline role of this library uses: one
+ * GPU thread waits on an mbarrier phase, with a limit of `limit_ns` (1 .. 1e8 ns).  With
+ * `arrive` == 0 nothing completes the phase, so the wait runs out, records MES_ERR_TIMEOUT
+ * (returned by the next mes_take_device_error) and the kernel returns normally - the
+ * context stays usable; with `arrive` != 0 the thread arrives first and nothing is
+ * recorded.  No counterpart in the reference, which has no device waits. */
+int mes_wait_probe(int64_t limit_ns, int arrive, void* stream);
+
 /* Leaves `sms` SMs (0..64) free of the persistent kernels (AWQ GEMM, attention) so that
  * another kernel running concurrently - an NCCL all-reduce overlapped on its own stream -
  * delays none of their CTAs.  Process-wide; 0 (the default) uses every SM.  No counterpart
@@ -151,9 +159,11 @@ int mes_varlen_attention(const void* qkv, int64_t ld, void* out, const void* wor
  * device memory is fixed in advance by its own pool).  No counterpart in the reference.
  * The workspace is a fixed array inside this library, on every device that loads it,
  * sized for at most mes_varlen_attention_noalloc_max_tokens() tokens (131072, ~1.5 MiB);
- * larger T returns MES_ERR_INVALID.  Nothing is allocated.  The first call on a device
- * looks up the array's device address (make that first call before any stream capture).
- * Every call on a device shares the array: calls whose GPU work overlaps race.
+ * larger T returns MES_ERR_INVALID.  Nothing is allocated.  The first call in each CUDA
+ * context of a device (and the first after the device's current context changed, e.g.
+ * after cudaDeviceReset) looks up the array's device address: make that call before any
+ * stream capture.  Every call on a device shares the array: calls whose GPU work overlaps
+ * race.
  * positions: i64 [T]; qkv, out, D, scale as for mes_varlen_attention.
  * ------------------------------------------------------------------------------- */
 int64_t mes_varlen_attention_noalloc_max_tokens(void);
@@ -220,6 +230,22 @@ int mes_awq_gemm_residual(const void* X, int64_t ldx, const int32_t* qweight_mes
                           const int32_t* qzeros, const void* scales, const void* bias, float* R,
                           int64_t ldr, int64_t M, int64_t N, int64_t K, int group_size,
                           void* stream);
+
+/* The three GEMMs above with a caller-provided workspace, selected by `epilogue`:
+ * 0 = mes_awq_gemm (Y bf16 [M, N]), 1 = mes_awq_gemm_residual (Y = R, f32 [M, N], +=),
+ * 2 = mes_awq_gemm_silu (Y bf16 [M, N/2], bias must be NULL).  Same computation and
+ * requirements; the same three projections of layers/linear.py:90-180 are replaced.
+ * With a workspace of at least mes_awq_gemm_workspace_size(M, N, K) bytes (16-byte
+ * aligned), large batches first dequantise the weights once into a bf16 panel W^T [N, K]
+ * held there (same exact dequantisation) and then run the tensor-core mainloop on that
+ * panel, instead of dequantising again in every token tile.  A NULL or smaller workspace
+ * runs the fused kernels of the three entry points above.  The workspace is scratch:
+ * its contents are undefined after the call. */
+int64_t mes_awq_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
+int mes_awq_gemm_ws(int epilogue, const void* X, int64_t ldx, const int32_t* qweight_mes,
+                    const int32_t* qzeros, const void* scales, const void* bias, void* Y,
+                    int64_t ldy, int64_t M, int64_t N, int64_t K, int group_size,
+                    void* workspace, int64_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

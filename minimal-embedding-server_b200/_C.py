@@ -23,6 +23,7 @@ SIGNATURES = {
     "mes_status_string": (ctypes.c_char_p, [_i32]),
     "mes_take_device_error": (_i32, [ctypes.POINTER(_i32)]),
     "mes_set_sm_reserve": (_i32, [_i32]),
+    "mes_wait_probe": (_i32, [_i64, _i32, _vp]),
     "mes_embedding": (_i32, [_vp, _i64, _vp, _i64, _i64, _vp, _vp]),
     "mes_embedding_f32": (_i32, [_vp, _i64, _vp, _i64, _i64, _vp, _vp]),
     "mes_rmsnorm": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _vp]),
@@ -47,6 +48,9 @@ SIGNATURES = {
     "mes_awq_gemm_residual": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                      _i32, _vp]),
     "mes_awq_gemm_silu": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp]),
+    "mes_awq_gemm_workspace_size": (_i64, [_i64, _i64, _i64]),
+    "mes_awq_gemm_ws": (_i32, [_i32, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                               _i32, _vp, _i64, _vp]),
 }
 
 _lib = None
@@ -297,6 +301,35 @@ def awq_dequant(qweight_mes: torch.Tensor, qzeros: torch.Tensor, scales: torch.T
     return out
 
 
+# Epilogue selectors of mes_awq_gemm_ws.
+EPI_BF16, EPI_RESIDUAL, EPI_SILU = 0, 1, 2
+_EPI_NAME = {EPI_BF16: "bf16", EPI_RESIDUAL: "residual", EPI_SILU: "silu"}
+
+# Whether the GEMM wrappers hand the library a weight-panel workspace (taken from the torch
+# caching allocator, or from a CUDA graph's pool during capture).  Without one the library
+# runs its fused dequantising kernels for every M.
+use_gemm_workspace = True
+
+
+def _awq_gemm_call(epi: int, x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
+                   scales: torch.Tensor, bias, y: torch.Tensor, group_size: int) -> None:
+    K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
+    M = x.shape[0]
+    ws_bytes = int(lib().mes_awq_gemm_workspace_size(M, N, K)) if use_gemm_workspace else 0
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes > 0 else None
+    ev = gemm_events if gemm_event_kinds is None or _EPI_NAME[epi] in gemm_event_kinds else None
+    if ev is not None:
+        e0, e1 = _timing_event(), _timing_event()
+        e0.record()
+    _check(lib().mes_awq_gemm_ws(epi, _p(x), x.stride(0), _p(qweight_mes), _p(qzeros),
+                                 _p(scales), _p(bias), _p(y), y.stride(0), M, N, K, group_size,
+                                 _p(ws), ws_bytes, _stream(x)),
+           f"mes_awq_gemm ({_EPI_NAME[epi]} epilogue)", 2 if ws is not None else 1)
+    if ev is not None:
+        e1.record()
+        ev.append((e0, e1, 2.0 * M * N * K, (_EPI_NAME[epi], M, N, K)))
+
+
 def awq_gemm_residual(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
                       scales: torch.Tensor, residual: torch.Tensor,
                       bias: torch.Tensor | None = None, group_size: int = 128) -> torch.Tensor:
@@ -307,16 +340,7 @@ def awq_gemm_residual(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.
     K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
     M = x.shape[0]
     _need(x.shape[1] == K and tuple(residual.shape) == (M, N), "shape mismatch")
-    ev = gemm_events if gemm_event_kinds is None or "residual" in gemm_event_kinds else None
-    if ev is not None:
-        e0, e1 = _timing_event(), _timing_event()
-        e0.record()
-    _check(lib().mes_awq_gemm_residual(_p(x), x.stride(0), _p(qweight_mes), _p(qzeros),
-                                       _p(scales), _p(bias), _p(residual), residual.stride(0),
-                                       M, N, K, group_size, _stream(x)), "mes_awq_gemm_residual")
-    if ev is not None:
-        e1.record()
-        ev.append((e0, e1, 2.0 * M * N * K, ("residual", M, N, K)))
+    _awq_gemm_call(EPI_RESIDUAL, x, qweight_mes, qzeros, scales, bias, residual, group_size)
     return residual
 
 
@@ -332,16 +356,7 @@ def awq_gemm_silu(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tens
     _need(x.shape[1] == K, f"x has K={x.shape[1]}, weight has K={K}")
     if out is None:
         out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=x.device)
-    ev = gemm_events if gemm_event_kinds is None or "silu" in gemm_event_kinds else None
-    if ev is not None:
-        e0, e1 = _timing_event(), _timing_event()
-        e0.record()
-    _check(lib().mes_awq_gemm_silu(_p(x), x.stride(0), _p(qweight_mes), _p(qzeros), _p(scales),
-                                   _p(out), out.stride(0), M, N, K, group_size, _stream(x)),
-           "mes_awq_gemm_silu")
-    if ev is not None:
-        e1.record()
-        ev.append((e0, e1, 2.0 * M * N * K, ("silu", M, N, K)))
+    _awq_gemm_call(EPI_SILU, x, qweight_mes, qzeros, scales, None, out, group_size)
     return out
 
 
@@ -370,14 +385,5 @@ def awq_gemm(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
     _need(x.shape[1] == K, f"x has K={x.shape[1]}, weight has K={K}")
     if out is None:
         out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
-    ev = gemm_events if gemm_event_kinds is None or "bf16" in gemm_event_kinds else None
-    if ev is not None:
-        e0, e1 = _timing_event(), _timing_event()
-        e0.record()
-    _check(lib().mes_awq_gemm(_p(x), x.stride(0), _p(qweight_mes), _p(qzeros), _p(scales),
-                              _p(bias), _p(out), out.stride(0), M, N, K, group_size,
-                              _stream(x)), "mes_awq_gemm")
-    if ev is not None:
-        e1.record()
-        ev.append((e0, e1, 2.0 * M * N * K, ("bf16", M, N, K)))
+    _awq_gemm_call(EPI_BF16, x, qweight_mes, qzeros, scales, bias, out, group_size)
     return out

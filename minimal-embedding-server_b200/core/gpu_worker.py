@@ -12,12 +12,22 @@ post-processes, as in the reference.
 
 CUDA graphs.  A forward launches about 230 kernels (twice that with the tensor-parallel
 micro-batch overlap), and issuing them from Python costs about 60 us each - as much as the
-GPU time of a whole forward once it is split 4 or 8 ways.  So ``_inference`` captures the
-forward of each batch shape it meets - the token count and, at tp > 1, the micro-batch
-boundary - into a CUDA graph (NCCL collectives included) and replays it for later batches
-of that shape; the device schedule of each batch (sequence starts, attention work list)
-is computed inside the graph from the new positions.  Host (numpy) inputs take this path;
-device tensors, whose boundaries would need a host read, run eagerly.
+GPU time of a whole forward once it is split 4 or 8 ways.  So host (numpy) batches run as
+captured CUDA graphs (NCCL collectives included); the device schedule of each batch
+(sequence starts, attention work list) is computed inside the graph from the new
+positions, so one graph serves every batch of its token layout.
+
+The engine's batcher packs whole requests up to a token budget
+(``core/tokenizer_manager.py:98-139``), so the token count T varies from batch to batch.
+A graph is therefore keyed on a *bucketed* layout: the batch (each tensor-parallel
+micro-batch separately) is padded up to the next bucket size (multiples of 256 tokens up
+to 4096, of 1024 up to 32768, of 4096 beyond) with dummy sequences of at most 128 tokens,
+whose rows are never pooled and cost almost no attention.  A new T then reuses the graph of
+its bucket; a T that repeats gets a graph of its exact layout on its second occurrence (no
+padding at all).  Every row of a real token is computed exactly as in the unpadded forward
+(row results of every kernel are independent of the other rows of batches of more than 256
+tokens, and the dummy sequences attend only to themselves).  All graphs share one memory
+pool, so holding several costs the memory of the largest, not their sum.
 """
 from __future__ import annotations
 
@@ -33,6 +43,8 @@ from .. import _C
 from ..models.qwen2 import DecoderModel
 from ..models.registry import get_model_class
 
+PAD_SEQ = 128   # longest dummy sequence used for padding
+
 
 def tp_nccl_environment(world_size: int | None = None) -> None:
     """Call before ``init_process_group`` at tensor parallelism > 1 (``world_size``
@@ -42,6 +54,55 @@ def tp_nccl_environment(world_size: int | None = None) -> None:
     collective inside them.  Settings already in the environment win."""
     world = int(world_size if world_size is not None else os.environ.get("WORLD_SIZE", "1"))
     os.environ.setdefault("NCCL_MAX_NCHANNELS", str(max(DecoderModel.overlap_reserved_sms(world), 1)))
+
+
+def token_bucket(n: int) -> int:
+    """Padded token count of a (micro-)batch of ``n`` tokens: the next multiple of 256 up
+    to 4096, of 1024 up to 32768, of 4096 beyond (at most ~6% padding, ~3% typical)."""
+    step = 256 if n <= 4096 else 1024 if n <= 32768 else 4096
+    return max(step, -(-n // step) * step)
+
+
+class Layout:
+    """Where the tokens of a host batch go in the (padded) device batch.
+
+    ``parts``: ``(src_start, src_end, dst_start, padded_len)`` per micro-batch (one part
+    unsplit, two at tp > 1 when the batch is split at a sequence boundary); ``split``: the
+    device micro-batch boundary handed to the model (``DecoderModel.NO_SPLIT`` when
+    unsplit)."""
+
+    def __init__(self, parts, split: int):
+        self.parts = tuple(parts)
+        self.split = split
+        self.total = sum(p[3] for p in self.parts)
+        self.padded = any(p[1] - p[0] != p[3] for p in self.parts)
+
+    @property
+    def key(self):
+        return (tuple(p[3] for p in self.parts), self.split)
+
+    def pad(self, ids: np.ndarray, pos: np.ndarray):
+        """Padded copies of ``ids`` / ``positions`` (dummy sequences of <= PAD_SEQ tokens,
+        id 0, positions restarting at 0 so that each starts a new sequence)."""
+        if not self.padded:
+            return ids, pos
+        out_ids = np.zeros(self.total, dtype=np.int64)
+        out_pos = np.empty(self.total, dtype=np.int64)
+        for s0, s1, d0, n in self.parts:
+            m = s1 - s0
+            out_ids[d0:d0 + m] = ids[s0:s1]
+            out_pos[d0:d0 + m] = pos[s0:s1]
+            out_pos[d0 + m:d0 + n] = np.arange(n - m) % PAD_SEQ
+        return out_ids, out_pos
+
+    def rows(self, idx) -> np.ndarray:
+        """Device rows of host token indices ``idx``."""
+        idx = np.asarray(idx, dtype=np.int64)
+        out = idx.copy()
+        for s0, s1, d0, _ in self.parts:
+            sel = (idx >= s0) & (idx < s1)
+            out[sel] = idx[sel] - s0 + d0
+        return out
 
 
 class GPUWorker:
@@ -59,9 +120,14 @@ class GPUWorker:
                 model = get_model_class(mes_config.model_config)(mes_config)
         self.model = model.eval()
         self.use_cuda_graphs = os.environ.get("MES_CUDA_GRAPHS", "1") != "0"
-        self.max_graphs = 8
+        self.max_graphs = 32         # bucketed layouts kept (least recently used dropped)
+        self.max_exact_graphs = 4    # exact layouts of repeated token counts kept
         self._graphs: collections.OrderedDict = collections.OrderedDict()
+        self._exact: collections.OrderedDict = collections.OrderedDict()
+        self._seen: collections.Counter = collections.Counter()
         self._no_graph: set = set()
+        self._pool = None
+        self.captures = 0            # graphs captured so far (for tests and benchmarks)
 
     def _to_device(self, array) -> torch.Tensor:
         t = torch.from_numpy(np.ascontiguousarray(array)) if isinstance(array, np.ndarray) else array
@@ -69,68 +135,127 @@ class GPUWorker:
             t = t.pin_memory().to(self.device, non_blocking=True)
         return t
 
-    @torch.no_grad()
-    def _inference(self, input_ids, positions) -> torch.Tensor:
-        host = not (isinstance(positions, torch.Tensor) and positions.is_cuda)
-        if self.use_cuda_graphs and host:
-            pos_h = np.asarray(positions.numpy() if isinstance(positions, torch.Tensor) else positions)
-            split = DecoderModel.overlap_split_host(pos_h)
-            key = (int(pos_h.shape[0]), split)
-            if key not in self._no_graph:
-                g = self._graph_for(key, input_ids, positions)
-                if g is not None:
-                    graph, ids_s, pos_s, out = g
-                    ids_s.copy_(self._to_device(input_ids).to(torch.int64), non_blocking=True)
-                    pos_s.copy_(self._to_device(positions).to(torch.int64), non_blocking=True)
-                    graph.replay()
-                    return out
-        input_ids = self._to_device(input_ids).to(torch.int64)
-        positions = self._to_device(positions).to(torch.int64)
-        return self.model(input_ids=input_ids, positions=positions)
+    # ---------------------------------------------------------------- layouts and graphs
+    def layout(self, positions, exact: bool = False) -> Layout:
+        """Device layout of a host batch: its micro-batch boundary (tp > 1) and, unless
+        ``exact``, each micro-batch padded to its token bucket."""
+        pos = np.asarray(positions)
+        T = int(pos.shape[0])
+        split = DecoderModel.overlap_split_host(pos)
+        if split == DecoderModel.NO_SPLIT:
+            spans = [(0, T)]
+        else:
+            spans = [(0, split), (split, T)]
+        parts, d0 = [], 0
+        for s0, s1 in spans:
+            n = s1 - s0 if exact else token_bucket(s1 - s0)
+            parts.append((s0, s1, d0, n))
+            d0 += n
+        dev_split = DecoderModel.NO_SPLIT if len(parts) == 1 else parts[1][2]
+        return Layout(parts, dev_split)
 
-    def _graph_for(self, key, input_ids, positions):
-        """The captured forward for batch shape ``key`` (captured on first use, least
-        recently used dropped beyond ``max_graphs``); None if capture failed."""
-        g = self._graphs.get(key)
+    def _graph_layout(self, positions) -> Layout:
+        """Layout to run a host batch with: exact when its graph exists or its token layout
+        was seen before (it repeats), else bucketed."""
+        exact = self.layout(positions, exact=True)
+        if exact.key in self._exact:
+            return exact
+        self._seen[exact.key] += 1
+        if self._seen[exact.key] >= 2 or not self.layout(positions).padded:
+            return exact
+        return self.layout(positions)
+
+    def _graph_for(self, lay: Layout, ids, pos):
+        """The captured forward of layout ``lay`` (captured on first use); None if capture
+        failed (that layout then runs eagerly)."""
+        cache, limit = (self._graphs, self.max_graphs) if lay.padded else (self._exact, self.max_exact_graphs)
+        g = cache.get(lay.key)
         if g is not None:
-            self._graphs.move_to_end(key)
+            cache.move_to_end(lay.key)
             return g
         try:
-            g = self.capture(key[0], key[1], input_ids, positions)
+            g = self.capture(lay, ids, pos)
         except Exception as exc:   # an unsupported capture runs eagerly from now on
-            warnings.warn(f"CUDA-graph capture of a {key[0]}-token batch failed ({exc!r}); "
-                          "batches of this shape run eagerly", RuntimeWarning, stacklevel=2)
-            self._no_graph.add(key)
+            warnings.warn(f"CUDA-graph capture of a {lay.total}-token batch failed ({exc!r}); "
+                          "batches of this layout run eagerly", RuntimeWarning, stacklevel=2)
+            self._no_graph.add(lay.key)
             return None
-        self._graphs[key] = g
-        while len(self._graphs) > self.max_graphs:
-            self._graphs.popitem(last=False)
+        cache[lay.key] = g
+        while len(cache) > limit:
+            cache.popitem(last=False)
         return g
 
     @torch.no_grad()
-    def capture(self, T: int, split, input_ids, positions):
-        """Capture one forward of a ``T``-token batch (micro-batch boundary ``split``) into a
-        CUDA graph with its own memory pool.  Returns ``(graph, ids, positions, out)``: the
-        static input buffers to fill before ``graph.replay()`` and the output it writes.
-        ``input_ids`` / ``positions`` are a batch of that shape, run once eagerly first."""
-        ids_s = torch.empty(T, dtype=torch.int64, device=self.device)
-        pos_s = torch.empty(T, dtype=torch.int64, device=self.device)
-        ids_s.copy_(self._to_device(input_ids).to(torch.int64))
-        pos_s.copy_(self._to_device(positions).to(torch.int64))
+    def capture(self, lay: Layout, input_ids, positions):
+        """Capture one forward of layout ``lay`` into a CUDA graph (memory from the worker's
+        shared graph pool).  Returns ``(graph, ids, positions, out)``: the static device
+        input buffers to fill (padded) before ``graph.replay()`` and the ``[lay.total, H]``
+        output it writes.  ``input_ids`` / ``positions``: a host batch of that layout (not
+        yet padded), run once eagerly first."""
+        ids_h, pos_h = lay.pad(np.asarray(input_ids), np.asarray(positions))
+        ids_s = torch.empty(lay.total, dtype=torch.int64, device=self.device)
+        pos_s = torch.empty(lay.total, dtype=torch.int64, device=self.device)
+        ids_s.copy_(self._to_device(ids_h))
+        pos_s.copy_(self._to_device(pos_h))
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(side):
-            self.model(ids_s, pos_s, overlap_split=split)
+            self.model(ids_s, pos_s, overlap_split=lay.split)
         torch.cuda.current_stream(self.device).wait_stream(side)
+        if self._pool is None:
+            self._pool = torch.cuda.graph_pool_handle()
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            out = self.model(ids_s, pos_s, overlap_split=split)
+        with torch.cuda.graph(graph, pool=self._pool):
+            out = self.model(ids_s, pos_s, overlap_split=lay.split)
+        self.captures += 1
         return graph, ids_s, pos_s, out
+
+    def release_graphs(self) -> None:
+        """Drop every captured graph (required before the process group is destroyed when
+        the graphs hold NCCL work)."""
+        self._graphs.clear()
+        self._exact.clear()
+
+    # ---------------------------------------------------------------- forward
+    @torch.no_grad()
+    def _forward(self, input_ids, positions):
+        """Forward of one batch: ``(hidden, layout)`` where ``hidden`` holds the model
+        output in the device layout (``layout.rows`` maps host token indices to its rows;
+        ``layout`` is None for an unpadded eager forward)."""
+        host = not (isinstance(positions, torch.Tensor) and positions.is_cuda)
+        if self.use_cuda_graphs and host:
+            ids_h = np.asarray(input_ids.numpy() if isinstance(input_ids, torch.Tensor) else input_ids)
+            pos_h = np.asarray(positions.numpy() if isinstance(positions, torch.Tensor) else positions)
+            lay = self._graph_layout(pos_h)
+            if lay.key not in self._no_graph:
+                g = self._graph_for(lay, ids_h, pos_h)
+                if g is not None:
+                    graph, ids_s, pos_s, out = g
+                    ids_p, pos_p = lay.pad(ids_h, pos_h)
+                    ids_s.copy_(self._to_device(ids_p), non_blocking=True)
+                    pos_s.copy_(self._to_device(pos_p), non_blocking=True)
+                    graph.replay()
+                    return out, lay
+        input_ids = self._to_device(input_ids).to(torch.int64)
+        positions = self._to_device(positions).to(torch.int64)
+        return self.model(input_ids=input_ids, positions=positions), None
+
+    @torch.no_grad()
+    def _inference(self, input_ids, positions) -> torch.Tensor:
+        """``[T, H]`` hidden states of the batch (``gpu_worker.py:216-222``).  With CUDA
+        graphs the result lives in the graph's output buffer: it is overwritten by the
+        next call."""
+        out, lay = self._forward(input_ids, positions)
+        if lay is None or not lay.padded:
+            return out
+        if len(lay.parts) == 1:
+            return out[: lay.parts[0][1]]
+        return torch.cat([out[d0:d0 + (s1 - s0)] for s0, s1, d0, _ in lay.parts])
 
     @torch.no_grad()
     def postprocess(self, outputs: torch.Tensor, last_token_indices) -> torch.Tensor:
         """fp32 ``[B, H]`` host tensor of L2-normalised last-token states."""
-        idx = self._to_device(torch.as_tensor(last_token_indices, dtype=torch.int64))
+        idx = self._to_device(torch.as_tensor(np.asarray(last_token_indices), dtype=torch.int64))
         emb = _C.last_token_l2(outputs, idx)
         host = torch.empty(emb.shape, dtype=torch.float32, pin_memory=True)
         host.copy_(emb, non_blocking=True)
@@ -138,7 +263,10 @@ class GPUWorker:
         return host
 
     def embed(self, input_ids, positions, last_token_indices) -> torch.Tensor:
-        return self.postprocess(self._inference(input_ids, positions), last_token_indices)
+        out, lay = self._forward(input_ids, positions)
+        if lay is not None and lay.padded:
+            last_token_indices = lay.rows(last_token_indices)
+        return self.postprocess(out, last_token_indices)
 
     def embed_list(self, input_ids, positions, last_token_indices) -> list[list[float]]:
         """The reference's wire format: one Python list of floats per sequence

@@ -30,23 +30,54 @@ constexpr int64_t workspace_bytes(int64_t T) {
 
 static __device__ __align__(256) unsigned char g_noalloc_workspace[workspace_bytes(kNoAllocMaxTokens)];
 
-// Device address of g_noalloc_workspace per device.  In host code the symbol's name is
-// only a stand-in, so the address is looked up once per device with that device current.
+// Device address of g_noalloc_workspace, cached per device together with the CUDA context
+// it was looked up in.  In host code the symbol's name is only a stand-in, so the address is
+// looked up with that device current: on the first call in a context (the primary context,
+// or one a caller created itself) and again whenever the current context of the device has
+// changed, for instance after cudaDeviceReset created a new primary context.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
 constexpr int kMaxDevices = 64;
-void* g_workspace_ptr[kMaxDevices] = {nullptr};
+struct WorkspaceAddr {
+  CUcontext ctx;
+  void* ptr;
+};
+WorkspaceAddr g_workspace[kMaxDevices] = {};
 std::mutex g_workspace_mu;
+
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
 
 int workspace_for_current_device(void** ptr) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MES_ERR_CUDA;
+  CtxGetCurrentFn get_ctx = ctx_get_current_fn();
+  CUcontext ctx = nullptr;
+  if (!get_ctx || get_ctx(&ctx) != CUDA_SUCCESS) return MES_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_workspace_mu);
-  if (g_workspace_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_workspace) != cudaSuccess || p == nullptr)
-      return MES_ERR_CUDA;
-    g_workspace_ptr[dev] = p;
+  WorkspaceAddr& w = g_workspace[dev];
+  if (ctx != nullptr && w.ptr != nullptr && w.ctx == ctx) {
+    *ptr = w.ptr;
+    return MES_OK;
   }
-  *ptr = g_workspace_ptr[dev];
+  // The lookup binds the device's primary context to this thread when it had none, so the
+  // context is read again afterwards.
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_workspace) != cudaSuccess || p == nullptr)
+    return MES_ERR_CUDA;
+  if (get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr) return MES_ERR_CUDA;
+  w.ctx = ctx;
+  w.ptr = p;
+  *ptr = p;
   return MES_OK;
 }
 

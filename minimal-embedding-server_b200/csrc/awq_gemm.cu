@@ -504,7 +504,7 @@ struct PCfg {
   static constexpr int kSmem = kOffBar + 512 + 1024;
   static constexpr int kTmemNeed = 2 * BT + AST * 32;
   static_assert(kSmem <= 232448, "shared memory budget");
-  static_assert((2 * SST + 2 * kASlots + 4) * 8 + 8 <= 512, "barrier area");
+  static_assert((2 * SST + 2 * kASlots + 5) * 8 + 8 <= 512, "barrier area");
   static_assert(kTmemNeed <= 512, "TMEM budget");
   static_assert(kSBytes == 256 && kZBytes == 64 && kWStage % 128 == 0, "stage layout");
   static_assert(BT % 16 == 0 && BT <= 256 && kXStage % 1024 == 0, "tile");
@@ -535,7 +535,8 @@ awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
   uint64_t* aempty = afull + C::kASlots;      // [kASlots] MMAs reading the A slot done
   uint64_t* acc_full = aempty + C::kASlots;   // [2] accumulator complete
   uint64_t* acc_empty = acc_full + 2;         // [2] accumulator drained
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* drain = acc_empty + 2;            // abort path: all issued MMAs completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
 
@@ -557,6 +558,7 @@ awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
       mes::mbar_init(&acc_full[b], 1);
       mes::mbar_init(&acc_empty[b], C::kEpiWarps);
     }
+    mes::mbar_init(drain, 1);
     *abort_flag = 0;
     mes::fence_barrier_init();
   }
@@ -601,8 +603,13 @@ awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
         }
       }
       if (!ok) {
-        const uint64_t t = mes::globaltimer_ns();  // let issued copies land
-        while (mes::globaltimer_ns() - t < 1000000ull) {
+        // Let the copies already issued (the last SST iterations at most) land before the
+        // CTA exits.
+        const uint64_t tstart = mes::globaltimer_ns();
+        for (int i = it - SST < 0 ? 0 : it - SST; i < it; ++i) {
+          while (!mes::mbar_try_wait(&full[i % SST], (i / SST) & 1) &&
+                 mes::globaltimer_ns() - tstart < mes::kWaitLimitNs) {
+          }
         }
       }
     }
@@ -647,8 +654,10 @@ awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
         mes::tc_commit(&acc_full[b]);
       }
       if (!ok) {
-        const uint64_t t = mes::globaltimer_ns();  // let issued MMAs finish
-        while (mes::globaltimer_ns() - t < 1000000ull) {
+        // Wait (bounded) until every MMA issued so far has completed.
+        mes::tc_commit(drain);
+        const uint64_t tstart = mes::globaltimer_ns();
+        while (!mes::mbar_try_wait(drain, 0) && mes::globaltimer_ns() - tstart < mes::kWaitLimitNs) {
         }
       }
     }
@@ -787,28 +796,46 @@ awq_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
 
 // ----------------------------------------------------------------------------------------
 // Pair variant (clusters of two CTAs on neighbouring SMs, tcgen05 cta_group::2).  A pair
-// computes a 256-feature x 256-token tile: CTA r dequantises features [128r, 128r + 128)
-// of the tile and stages tokens [128r, 128r + 128) of X; one MMA of M = 256, N = 256 in
-// the even CTA reads A's rows and B's rows from both CTAs' shared memory and leaves each
-// CTA's 128 features x 256 tokens in that CTA's TMEM.  Against the single-CTA kernel every
-// SM stages and reads half the X bytes per k-step (tensor-core operand reads 32 KB instead
-// of 48 KB, TMA writes 20.5 KB instead of 36.5 KB), which both lowers the shared-memory
-// traffic that bounds the single-CTA mainloop and makes room for a five-deep ring.
-// Roles per CTA are those of the single-CTA kernel; the MMA warp of the odd CTA only takes
-// part in the TMEM allocation.  Barriers:
-//   full_x[s]  (even CTA)  both X halves landed: expect_tx by the even producer, complete_tx
-//                          from both CTAs' loads; waited for by the even CTA's dequant warps,
-//                          so the MMA's wait on afull covers it;
-//   full_w[s]  (each CTA)  the CTA's weight words, scales and zeros landed;
-//   afull[s]   (even CTA)  A rows of both CTAs written: 4 dequant warps of each CTA arrive;
+// computes a 256-feature x 256-token tile: CTA r holds features [128r, 128r + 128) of the
+// tile as A and tokens [128r, 128r + 128) of X as B; one MMA of M = 256, N = 256 in the
+// even CTA reads A's rows and B's rows from both CTAs' shared memory and leaves each CTA's
+// 128 features x 256 tokens in that CTA's TMEM.  Against the single-CTA kernel every SM
+// stages and reads half the X bytes per k-step (tensor-core operand reads 32 KB instead of
+// 48 KB), which lowers the shared-memory traffic that bounds the single-CTA mainloop.
+//
+// Two ways to fill A (PANEL):
+//   false  dequant warps (SETS sets of four) turn the stage's packed weight words, scales
+//          and zeros (TMA-loaded per CTA) into the 128 x 64 A tile, as in the single-CTA
+//          kernel;
+//   true   A is TMA-loaded from a bf16 weight panel W^T [N, K] that awq_panel_kernel
+//          dequantised just before (same exact arithmetic).  No dequant warps: the
+//          mainloop is the tensor pipe and TMA alone, and the panel (N*K*2 bytes) is read
+//          from L2.
+// Roles per CTA: warp 0 TMA producer, warp 1 MMA issuer (even CTA only; the odd CTA's
+// warp 1 only takes part in the TMEM allocation), [dequant warps], 8 epilogue warps.
+// Barriers:
+//   full_x[s]  (even CTA)  both X halves landed (PANEL: both X and both A halves):
+//                          expect_tx by the even producer, complete_tx from both CTAs'
+//                          loads.  Fused: waited for by the even CTA's dequant warps, so
+//                          the MMA's wait on afull covers it; PANEL: waited for by the MMA;
+//   full_w[s]  (each CTA)  fused only: the CTA's weight words, scales and zeros landed;
+//   afull[s]   (even CTA)  fused only: A rows of both CTAs written (4 dequant warps of
+//                          each CTA arrive per set);
 //   empty[s]   (each CTA)  the stage's MMAs done (commit multicast to both CTAs);
 //   acc_full[b] (each CTA) accumulator b complete (commit multicast);
-//   acc_empty[b] (even CTA) accumulator b drained in both CTAs (8 epilogue warps each).
-template <int EPI>
+//   acc_empty[b] (even CTA) accumulator b drained in both CTAs (8 epilogue warps each);
+//   drain      (each CTA)  abort path only: every MMA issued so far has completed.
+// Tile order (pair_tile): feature tiles are grouped into bands of `band` tiles; the pairs
+// walk one band at a time, features fastest inside it.  A band's panel rows stay in L2
+// while every token tile passes them, and the X tiles of a token row are shared by the
+// pairs working on that row at the same time.
+template <int EPI, bool PANEL>
 struct QCfg {
   static constexpr bool kResidual = EPI == kEpiResidual, kSilu = EPI == kEpiSilu;
-  // The residual epilogue stages nothing in shared memory, which leaves room for a sixth stage.
-  static constexpr int SST = kResidual ? 6 : 5, SETS = 2;
+  static constexpr int SETS = PANEL ? 0 : 2;
+  // The residual epilogue stages nothing in shared memory, which leaves room for one more
+  // stage; the panel variant's stages have no weight words.
+  static constexpr int SST = PANEL ? (kResidual ? 7 : 6) : (kResidual ? 6 : 5);
   static constexpr int kDqWarps = 4 * SETS;
   static constexpr int kEpiWarps = 8;
   static constexpr int kThreads = (2 + kDqWarps + kEpiWarps) * 32;
@@ -817,10 +844,10 @@ struct QCfg {
   static constexpr int kHalfT = kTileT / 2;
   static constexpr int kXStage = kHalfT * kBK * 2;
   static constexpr int kAStage = kBN * kBK * 2;
-  static constexpr int kWBytes = (kBK / 8) * kBN * 4;
+  static constexpr int kWBytes = PANEL ? 0 : (kBK / 8) * kBN * 4;
   static constexpr int kSBytes = kBN * 2;
   static constexpr int kZBytes = (kBN / 8) * 4;
-  static constexpr int kWStage = kWBytes + 256 + 128;
+  static constexpr int kWStage = PANEL ? 0 : kWBytes + 256 + 128;
   static constexpr int kChunk = kResidual ? 16 : 32;
   static constexpr int kOutBuf = kChunk * 32 * 2;
   static constexpr int kOffX = 0;
@@ -830,21 +857,31 @@ struct QCfg {
   static constexpr int kOffBar = kOffOut + (kResidual ? 0 : kEpiWarps * kOutBuf);
   static constexpr int kSmem = kOffBar + 512 + 1024;
   static_assert(kSmem <= 232448, "shared memory budget");
-  static_assert((4 * SST + 4) * 8 + 8 <= 512, "barrier area");
+  static_assert((4 * SST + 5) * 8 + 8 <= 512, "barrier area");
   static_assert(kSBytes == 256 && kZBytes == 64 && kWStage % 128 == 0, "stage layout");
   static_assert(kXStage % 1024 == 0 && kAStage % 1024 == 0, "swizzle atoms");
 };
 
-template <int EPI>
-__global__ void __launch_bounds__(QCfg<EPI>::kThreads, 1)
+// (feature tile, token tile) of pair tile `tile` in the banded order described above.
+__device__ __forceinline__ void pair_tile(int tile, int num_n, int num_t, int band, int& f,
+                                          int& t) {
+  const int per_band = band * num_t;
+  const int b = tile / per_band, r = tile - b * per_band;
+  const int width = min(band, num_n - b * band);
+  f = b * band + r % width;
+  t = r / width;
+}
+
+template <int EPI, bool PANEL>
+__global__ void __launch_bounds__(QCfg<EPI, PANEL>::kThreads, 1)
 awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
                      const __grid_constant__ CUtensorMap map_w,
                      const __grid_constant__ CUtensorMap map_s,
                      const __grid_constant__ CUtensorMap map_z,
                      const __grid_constant__ CUtensorMap map_y,
                      const __nv_bfloat16* __restrict__ bias, float* __restrict__ R, int64_t ldr,
-                     int M, int N, int K) {
-  using C = QCfg<EPI>;
+                     int M, int N, int K, int band) {
+  using C = QCfg<EPI, PANEL>;
   constexpr int SST = C::SST;
   constexpr uint32_t kTmemCols = 512;
   extern __shared__ uint8_t smem_raw[];
@@ -861,7 +898,8 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
   uint64_t* empty = bars + 3 * SST;     // [SST]
   uint64_t* acc_full = bars + 4 * SST;  // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* drain = acc_empty + 2;      // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = mes::warp_id(), lane = mes::lane_id();
@@ -869,7 +907,8 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int nk = K / kBK;
   const int num_n = N / C::kTileN;
-  const int num_tiles = num_n * ((M + C::kTileT - 1) / C::kTileT);
+  const int num_t = (M + C::kTileT - 1) / C::kTileT;
+  const int num_tiles = num_n * num_t;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SST; ++s) {
@@ -882,15 +921,18 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
       mes::mbar_init(&acc_full[b], 1);
       mes::mbar_init(&acc_empty[b], 2 * C::kEpiWarps);
     }
+    mes::mbar_init(drain, 1);
     *abort_flag = 0;
     mes::fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     mes::tma_prefetch_desc(&map_x);
     mes::tma_prefetch_desc(&map_w);
-    mes::tma_prefetch_desc(&map_s);
-    mes::tma_prefetch_desc(&map_z);
-    if (EPI == kEpiBf16) mes::tma_prefetch_desc(&map_y);
+    if constexpr (!PANEL) {
+      mes::tma_prefetch_desc(&map_s);
+      mes::tma_prefetch_desc(&map_z);
+    }
+    if (EPI != kEpiResidual) mes::tma_prefetch_desc(&map_y);
   }
   if (warp == 1) {
     __syncwarp();
@@ -909,8 +951,10 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
       int it = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-        const int n0 = (tile % num_n) * C::kTileN + (int)rank * kBN;
-        const int t0 = (tile / num_n) * C::kTileT + (int)rank * C::kHalfT;
+        int f, t;
+        pair_tile(tile, num_n, num_t, band, f, t);
+        const int n0 = f * C::kTileN + (int)rank * kBN;
+        const int t0 = t * C::kTileT + (int)rank * C::kHalfT;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % SST;
           if (it >= SST &&
@@ -918,18 +962,31 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
             ok = false;
             break;
           }
-          if (rank == 0) mes::mbar_arrive_expect_tx(&full_x[s], 2 * C::kXStage);
-          mes::tma_load_2d_pair(xs + s * C::kXStage, &map_x, full_x0 + 8 * s, kb * kBK, t0);
-          uint8_t* w = wst + s * C::kWStage;
-          mes::mbar_arrive_expect_tx(&full_w[s], C::kWBytes + C::kSBytes + C::kZBytes);
-          mes::tma_load_2d(w, &map_w, &full_w[s], n0, kb * (kBK / 8));
-          mes::tma_load_2d(w + C::kWBytes, &map_s, &full_w[s], n0, kb / 2);
-          mes::tma_load_2d(w + C::kWBytes + 256, &map_z, &full_w[s], n0 / 8, kb / 2);
+          if constexpr (PANEL) {
+            if (rank == 0) mes::mbar_arrive_expect_tx(&full_x[s], 2 * (C::kXStage + C::kAStage));
+            mes::tma_load_2d_pair(as + s * C::kAStage, &map_w, full_x0 + 8 * s, kb * kBK, n0);
+            mes::tma_load_2d_pair(xs + s * C::kXStage, &map_x, full_x0 + 8 * s, kb * kBK, t0);
+          } else {
+            if (rank == 0) mes::mbar_arrive_expect_tx(&full_x[s], 2 * C::kXStage);
+            mes::tma_load_2d_pair(xs + s * C::kXStage, &map_x, full_x0 + 8 * s, kb * kBK, t0);
+            uint8_t* w = wst + s * C::kWStage;
+            mes::mbar_arrive_expect_tx(&full_w[s], C::kWBytes + C::kSBytes + C::kZBytes);
+            mes::tma_load_2d(w, &map_w, &full_w[s], n0, kb * (kBK / 8));
+            mes::tma_load_2d(w + C::kWBytes, &map_s, &full_w[s], n0, kb / 2);
+            mes::tma_load_2d(w + C::kWBytes + 256, &map_z, &full_w[s], n0 / 8, kb / 2);
+          }
         }
       }
       if (!ok) {
-        const uint64_t t = mes::globaltimer_ns();  // let issued copies land
-        while (mes::globaltimer_ns() - t < 1000000ull) {
+        // Let the copies already issued land before the CTA exits: the even CTA's full_x
+        // counts both CTAs' pair copies of every stage it armed, full_w this CTA's own
+        // copies.  (The cluster barrier at the end keeps the odd CTA until then.)
+        const uint64_t tstart = mes::globaltimer_ns();
+        for (int i = it - SST < 0 ? 0 : it - SST; i < it; ++i) {
+          while (((rank == 0 && !mes::mbar_try_wait(&full_x[i % SST], (i / SST) & 1)) ||
+                  (!PANEL && !mes::mbar_try_wait(&full_w[i % SST], (i / SST) & 1))) &&
+                 mes::globaltimer_ns() - tstart < mes::kWaitLimitNs) {
+          }
         }
       }
     }
@@ -951,9 +1008,10 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
         mes::tc_fence_after();
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % SST;
-          // afull implies full_x: the even CTA's dequant warps wait for both X halves before
-          // arriving, so one barrier check per k-step suffices.
-          if (!mes::mbar_wait(&afull[s], (it / SST) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
+          // Fused: afull implies full_x (the even CTA's dequant warps wait for both X halves
+          // before arriving), so one barrier check per k-step suffices.
+          uint64_t* ready = PANEL ? &full_x[s] : &afull[s];
+          if (!mes::mbar_wait(ready, (it / SST) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
             ok = false;
             break;
           }
@@ -969,57 +1027,61 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
         if (ok) mes::tc_commit2_mc(&acc_full[b], 0x3);
       }
       if (!ok) {
-        const uint64_t t = mes::globaltimer_ns();  // let issued MMAs finish
-        while (mes::globaltimer_ns() - t < 1000000ull) {
+        // Wait (bounded) until every MMA issued so far has completed.
+        mes::tc_commit2_mc(drain, 0x1);
+        const uint64_t tstart = mes::globaltimer_ns();
+        while (!mes::mbar_try_wait(drain, 0) && mes::globaltimer_ns() - tstart < mes::kWaitLimitNs) {
         }
       }
     }
     __syncwarp();
   } else if (warp < 2 + C::kDqWarps) {
-    // --------------------------------- dequant ----------------------------------------
-    const int set = (warp - 2) / 4;
-    const int row = (warp & 3) * 32 + lane;
-    const int zshift = 4 * kInvOrder[row & 7];  // n0 is a multiple of 128
-    const uint32_t afull0 = mes::mapa_shared(mes::smem_u32(afull), 0);
-    int it = 0;
-    bool ok = true;
-    for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-      for (int kb = 0; kb < nk; ++kb, ++it) {
-        if (it % C::SETS != set) continue;
-        const int s = it % SST;
-        // The A slot of a stage is free once the stage's weights landed again: the producer
-        // refills a stage only after its MMAs completed.
-        if (!mes::mbar_wait_warp(&full_w[s], (it / SST) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT) ||
-            (rank == 0 &&
-             !mes::mbar_wait_warp(&full_x[s], (it / SST) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT))) {
-          ok = false;
-          break;
-        }
-        const uint8_t* w = wst + s * C::kWStage;
-        const GroupParams gp =
-            make_group(reinterpret_cast<const uint32_t*>(w + C::kWBytes + 256)[row >> 3], zshift,
-                       reinterpret_cast<const uint16_t*>(w + C::kWBytes)[row]);
-        const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(w) + row;
-        uint32_t av[32];
+    // --------------------------------- dequant (fused only) ---------------------------
+    if constexpr (!PANEL) {
+      const int set = (warp - 2) / 4;
+      const int row = (warp & 3) * 32 + lane;
+      const int zshift = 4 * kInvOrder[row & 7];  // n0 is a multiple of 128
+      const uint32_t afull0 = mes::mapa_shared(mes::smem_u32(afull), 0);
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          if (it % C::SETS != set) continue;
+          const int s = it % SST;
+          // The A slot of a stage is free once the stage's weights landed again: the
+          // producer refills a stage only after its MMAs completed.
+          if (!mes::mbar_wait_warp(&full_w[s], (it / SST) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT) ||
+              (rank == 0 &&
+               !mes::mbar_wait_warp(&full_x[s], (it / SST) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT))) {
+            ok = false;
+            break;
+          }
+          const uint8_t* w = wst + s * C::kWStage;
+          const GroupParams gp =
+              make_group(reinterpret_cast<const uint32_t*>(w + C::kWBytes + 256)[row >> 3], zshift,
+                         reinterpret_cast<const uint16_t*>(w + C::kWBytes)[row]);
+          const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(w) + row;
+          uint32_t av[32];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint32_t v = wsrc[i * kBN];
-          av[4 * i + 0] = dq_pair(v, gp);
-          av[4 * i + 1] = dq_pair(v >> 4, gp);
-          av[4 * i + 2] = dq_pair(v >> 8, gp);
-          av[4 * i + 3] = dq_pair(v >> 12, gp);
-        }
-        // Row `row` of the 128 x 64 K-major tile, 128-byte swizzle: 16-byte chunk i
-        // (k = 8i .. 8i+7) lives at chunk position i ^ (row & 7).
-        uint8_t* arow = as + s * C::kAStage + row * 128;
+          for (int i = 0; i < 8; ++i) {
+            const uint32_t v = wsrc[i * kBN];
+            av[4 * i + 0] = dq_pair(v, gp);
+            av[4 * i + 1] = dq_pair(v >> 4, gp);
+            av[4 * i + 2] = dq_pair(v >> 8, gp);
+            av[4 * i + 3] = dq_pair(v >> 12, gp);
+          }
+          // Row `row` of the 128 x 64 K-major tile, 128-byte swizzle: 16-byte chunk i
+          // (k = 8i .. 8i+7) lives at chunk position i ^ (row & 7).
+          uint8_t* arow = as + s * C::kAStage + row * 128;
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          *reinterpret_cast<uint4*>(arow + ((i ^ (row & 7)) * 16)) =
-              make_uint4(av[4 * i], av[4 * i + 1], av[4 * i + 2], av[4 * i + 3]);
-        mes::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mes::mbar_arrive_remote(afull0 + 8 * s);
-        __syncwarp();
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<uint4*>(arow + ((i ^ (row & 7)) * 16)) =
+                make_uint4(av[4 * i], av[4 * i + 1], av[4 * i + 2], av[4 * i + 3]);
+          mes::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mes::mbar_arrive_remote(afull0 + 8 * s);
+          __syncwarp();
+        }
       }
     }
   } else {
@@ -1033,8 +1095,10 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
     int lt = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs, ++lt) {
       const int b = lt & 1;
-      const int n0 = (tile % num_n) * C::kTileN + (int)rank * kBN;
-      const int t0 = (tile / num_n) * C::kTileT;
+      int f, t;
+      pair_tile(tile, num_n, num_t, band, f, t);
+      const int n0 = f * C::kTileN + (int)rank * kBN;
+      const int t0 = t * C::kTileT;
       const int n = n0 + q * 32 + lane;
       if (!mes::mbar_wait_warp(&acc_full[b], (lt >> 1) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT))
         break;
@@ -1099,6 +1163,32 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
     mes::tc_fence_after();
     mes::tmem_dealloc2(tmem, kTmemCols);
   }
+}
+
+// ------------------------------------ weight panel ----------------------------------------
+// W^T [N, K] bf16 (K contiguous) from the kernel-layout AWQ tensors, with the GEMM's exact
+// dequantisation: the A operand of the PANEL pair kernel.  A block of 256 threads covers 8
+// features x 32 words (256 k): warp f takes feature n0 + f, lane b word b0 + b, so a warp
+// writes 512 contiguous bytes of its feature's row, and the eight warps read the same 32
+// sectors of the packed words (one per word row, eight features each) through L1.
+__global__ void __launch_bounds__(256) awq_panel_kernel(const uint32_t* __restrict__ qw,
+                                                        const int32_t* __restrict__ qzeros,
+                                                        const uint16_t* __restrict__ scales,
+                                                        int K, int N, uint4* __restrict__ out) {
+  const int f = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.y * 8 + f;
+  const int b = blockIdx.x * 32 + lane;
+  if (b >= K / 8) return;
+  const int g = (8 * b) / kGroup;
+  const GroupParams gp = make_group(__ldg(qzeros + (int64_t)g * (N / 8) + (n >> 3)),
+                                    4 * kInvOrder[n & 7], __ldg(scales + (int64_t)g * N + n));
+  const uint32_t w = __ldg(qw + (int64_t)b * N + n);
+  uint4 v;
+  v.x = dq_pair(w, gp);
+  v.y = dq_pair(w >> 4, gp);
+  v.z = dq_pair(w >> 8, gp);
+  v.w = dq_pair(w >> 12, gp);
+  out[(int64_t)n * (K / 8) + b] = v;
 }
 
 // ------------------------------------ repack ----------------------------------------------
@@ -1284,13 +1374,14 @@ int launch_gemm_persistent(const void* X, int64_t ldx, const int32_t* qw, const 
 }
 
 // Pair kernel launch: clusters of two CTAs, as many pairs as can be resident at once
-// (at most one per two SMs) and no more than there are pair tiles.
-template <int EPI>
-int launch_gemm_pair(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
+// (at most one per two SMs) and no more than there are pair tiles.  PANEL: `w` is the bf16
+// weight panel W^T [N, K] (qzeros / scales unused); otherwise the kernel-layout words.
+template <int EPI, bool PANEL>
+int launch_gemm_pair(const void* X, int64_t ldx, const void* w, const int32_t* qzeros,
                      const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
                      int64_t N, int64_t K, cudaStream_t stream) {
-  using C = QCfg<EPI>;
-  auto kern = awq_gemm_pair_kernel<EPI>;
+  using C = QCfg<EPI, PANEL>;
+  auto kern = awq_gemm_pair_kernel<EPI, PANEL>;
   static std::atomic<uint64_t> attr_done{0};
   const int st = mes_host::once_per_device(attr_done, [&] {
     return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) == cudaSuccess
@@ -1299,14 +1390,23 @@ int launch_gemm_pair(const void* X, int64_t ldx, const int32_t* qw, const int32_
   if (st != MES_OK) return st;
   CUtensorMap mx, mw, ms, mz, my;
   if (!mes_host::make_map_2d(&mx, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, ldx, C::kHalfT,
-                             kBK, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !mes_host::make_map_2d(&mw, qw, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, K / 8, N, N, kBK / 8, kBN,
-                             CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !mes_host::make_map_2d(&ms, scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, K / kGroup, N, N, 1,
-                             kBN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !mes_host::make_map_2d(&mz, qzeros, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, K / kGroup, N / 8,
-                             N / 8, 1, kBN / 8, CU_TENSOR_MAP_SWIZZLE_NONE))
+                             kBK, CU_TENSOR_MAP_SWIZZLE_128B))
     return MES_ERR_INVALID;
+  if constexpr (PANEL) {
+    if (!mes_host::make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, K, kBN, kBK,
+                               CU_TENSOR_MAP_SWIZZLE_128B))
+      return MES_ERR_INVALID;
+    ms = mw;  // unused by the panel variant
+    mz = mw;
+  } else {
+    if (!mes_host::make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, K / 8, N, N, kBK / 8, kBN,
+                               CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !mes_host::make_map_2d(&ms, scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, K / kGroup, N, N, 1,
+                               kBN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !mes_host::make_map_2d(&mz, qzeros, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, K / kGroup, N / 8,
+                               N / 8, 1, kBN / 8, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return MES_ERR_INVALID;
+  }
   if (!make_out_map(&my, mx, EPI, Y, M, N, ldy, C::kChunk)) return MES_ERR_INVALID;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -1330,14 +1430,45 @@ int launch_gemm_pair(const void* X, int64_t ldx, const int32_t* qw, const int32_
       return MES_ERR_CUDA;
     clusters_by_dev[dev & 63].store(clusters, std::memory_order_relaxed);
   }
-  const int64_t tiles = (N / C::kTileN) * ((M + C::kTileT - 1) / C::kTileT);
+  const int64_t num_n = N / C::kTileN;
+  const int64_t tiles = num_n * ((M + C::kTileT - 1) / C::kTileT);
   const int64_t max_pairs = clusters < mes_host::persistent_ctas() / 2 ? clusters : mes_host::persistent_ctas() / 2;
   const int64_t pairs = tiles < max_pairs ? tiles : max_pairs;
+  // Band of feature tiles walked at a time: the panel rows of a band (about 40 MB at most)
+  // stay in L2 while the token tiles pass them.  The packed weights are 4x smaller and are
+  // walked in one band.
+  int64_t band = num_n;
+  if (PANEL) {
+    band = (40ll << 20) / ((int64_t)C::kTileN * K * 2);
+    band = band < 1 ? 1 : (band > num_n ? num_n : band);
+  }
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mx, mw, ms, mz, my, (const __nv_bfloat16*)bias,
-                         C::kResidual || C::kSilu ? (float*)Y : nullptr, ldy, (int)M, (int)N, (int)K);
+                         C::kResidual || C::kSilu ? (float*)Y : nullptr, ldy, (int)M, (int)N, (int)K,
+                         (int)band);
   if (e != cudaSuccess) return MES_ERR_CUDA;
   return mes_host::from_cuda(cudaGetLastError());
+}
+
+// The weight panel W^T [N, K] bf16 of one GEMM (see awq_panel_kernel).
+int launch_panel(const int32_t* qw, const int32_t* qzeros, const void* scales, int64_t N,
+                 int64_t K, void* panel, cudaStream_t stream) {
+  const dim3 grid((unsigned)((K / 8 + 31) / 32), (unsigned)(N / 8), 1);
+  awq_panel_kernel<<<grid, 256, 0, stream>>>((const uint32_t*)qw, qzeros, (const uint16_t*)scales,
+                                            (int)K, (int)N, (uint4*)panel);
+  return mes_host::from_cuda(cudaGetLastError());
+}
+
+// Whether the GEMM of this shape takes the panel path when given a workspace: batches of
+// more than 256 tokens (the batches the persistent kernels serve), N a multiple of the pair
+// tile, and the panel grid within the launch limits.  MES_GEMM_PANEL=0 (read once) turns
+// the path off, for comparisons.
+bool panel_path(int64_t M, int64_t N, int64_t K) {
+  static const bool enabled = [] {
+    const char* v = getenv("MES_GEMM_PANEL");
+    return !(v && atoi(v) == 0);
+  }();
+  return enabled && M > 256 && N % (2 * kBN) == 0 && N / 8 <= 65535 && K <= (1 << 24);
 }
 
 // Tile configuration for M > 64 tokens.  The environment variable MES_GEMM_CONFIG (read
@@ -1366,7 +1497,7 @@ int large_m_config() {
 template <int EPI>
 int dispatch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
                   const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
-                  int64_t N, int64_t K, cudaStream_t s) {
+                  int64_t N, int64_t K, void* panel, int64_t panel_bytes, cudaStream_t s) {
   if (M <= 16) return launch_gemm<16, 16, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
   if (M <= 32) return launch_gemm<32, 11, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
   if (M <= 64) return launch_gemm<64, 7, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
@@ -1377,15 +1508,22 @@ int dispatch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* 
   // each output in the same order (a row's result does not depend on the batch around it).
   if (config == 2 || (config != 1 && M <= 256 && 2 * (N / kBN) <= mes_host::persistent_ctas()))
     return launch_gemm<256, 5, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  // Large M with a workspace: dequantise the weights once into a bf16 panel, then run the
+  // pair kernel on the panel, so no SM repeats the dequantisation per token tile.
+  if (panel && panel_path(M, N, K) && panel_bytes >= N * K * 2) {
+    const int st = launch_panel(qw, qzeros, scales, N, K, panel, s);
+    if (st != MES_OK) return st;
+    return launch_gemm_pair<EPI, true>(X, ldx, panel, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  }
   switch (config) {
     case 1: return launch_gemm_persistent<192, 4, 4, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
     case 3: return launch_gemm_persistent<256, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
     case 4:
-      if (N % (2 * kBN) == 0) return launch_gemm_pair<EPI>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+      if (N % (2 * kBN) == 0) return launch_gemm_pair<EPI, false>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
       return launch_gemm_persistent<256, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
     default:
       if (EPI == kEpiResidual && N % (2 * kBN) == 0)
-        return launch_gemm_pair<EPI>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+        return launch_gemm_pair<EPI, false>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
       return launch_gemm_persistent<256, 4, 0, EPI, 2>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
   }
 }
@@ -1440,38 +1578,58 @@ extern "C" int mes_awq_dequant(const int32_t* qweight_mes, const int32_t* qzeros
   return mes_host::from_cuda(cudaGetLastError());
 }
 
+extern "C" int64_t mes_awq_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0 || N % kBN || K % kGroup) return 0;
+  return panel_path(M, N, K) ? N * K * 2 : 0;
+}
+
+extern "C" int mes_awq_gemm_ws(int epilogue, const void* X, int64_t ldx, const int32_t* qweight_mes,
+                               const int32_t* qzeros, const void* scales, const void* bias, void* Y,
+                               int64_t ldy, int64_t M, int64_t N, int64_t K, int group_size,
+                               void* workspace, int64_t workspace_bytes, void* stream) {
+  if (epilogue < kEpiBf16 || epilogue > kEpiSilu || workspace_bytes < 0) return MES_ERR_INVALID;
+  if (epilogue == kEpiSilu && bias) return MES_ERR_INVALID;
+  const int st = check_gemm_args(X, ldx, qweight_mes, qzeros, scales, Y, ldy, M, N, K, group_size,
+                                 epilogue == kEpiResidual ? 1 : 8,
+                                 epilogue == kEpiSilu ? N / 2 : N);
+  if (st != MES_OK) return st < 0 ? MES_OK : st;
+  const bool y_ok = epilogue == kEpiResidual ? (reinterpret_cast<uintptr_t>(Y) & 3) == 0 : aligned16(Y);
+  if (!aligned16(X) || !aligned16(qweight_mes) || !y_ok) return MES_ERR_ALIGN;
+  if (workspace && !aligned16(workspace)) return MES_ERR_ALIGN;
+  if (!workspace) workspace_bytes = 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (epilogue) {
+    case kEpiBf16:
+      return dispatch_gemm<kEpiBf16>(X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K,
+                                     workspace, workspace_bytes, s);
+    case kEpiResidual:
+      return dispatch_gemm<kEpiResidual>(X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N,
+                                         K, workspace, workspace_bytes, s);
+    default:
+      return dispatch_gemm<kEpiSilu>(X, ldx, qweight_mes, qzeros, scales, nullptr, Y, ldy, M, N, K,
+                                     workspace, workspace_bytes, s);
+  }
+}
+
 extern "C" int mes_awq_gemm(const void* X, int64_t ldx, const int32_t* qweight_mes,
                             const int32_t* qzeros, const void* scales, const void* bias, void* Y,
                             int64_t ldy, int64_t M, int64_t N, int64_t K, int group_size,
                             void* stream) {
-  const int st = check_gemm_args(X, ldx, qweight_mes, qzeros, scales, Y, ldy, M, N, K,
-                                 group_size, 8, N);
-  if (st != MES_OK) return st < 0 ? MES_OK : st;
-  if (!aligned16(X) || !aligned16(Y) || !aligned16(qweight_mes)) return MES_ERR_ALIGN;
-  return dispatch_gemm<kEpiBf16>(X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K,
-                                 (cudaStream_t)stream);
+  return mes_awq_gemm_ws(kEpiBf16, X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K,
+                         group_size, nullptr, 0, stream);
 }
 
 extern "C" int mes_awq_gemm_residual(const void* X, int64_t ldx, const int32_t* qweight_mes,
                                      const int32_t* qzeros, const void* scales, const void* bias,
                                      float* R, int64_t ldr, int64_t M, int64_t N, int64_t K,
                                      int group_size, void* stream) {
-  const int st = check_gemm_args(X, ldx, qweight_mes, qzeros, scales, R, ldr, M, N, K,
-                                 group_size, 1, N);
-  if (st != MES_OK) return st < 0 ? MES_OK : st;
-  if (!aligned16(X) || !aligned16(qweight_mes) || (reinterpret_cast<uintptr_t>(R) & 3))
-    return MES_ERR_ALIGN;
-  return dispatch_gemm<kEpiResidual>(X, ldx, qweight_mes, qzeros, scales, bias, R, ldr, M, N, K,
-                                     (cudaStream_t)stream);
+  return mes_awq_gemm_ws(kEpiResidual, X, ldx, qweight_mes, qzeros, scales, bias, R, ldr, M, N, K,
+                         group_size, nullptr, 0, stream);
 }
 
 extern "C" int mes_awq_gemm_silu(const void* X, int64_t ldx, const int32_t* qweight_mes,
                                  const int32_t* qzeros, const void* scales, void* Y, int64_t ldy,
                                  int64_t M, int64_t N, int64_t K, int group_size, void* stream) {
-  const int st = check_gemm_args(X, ldx, qweight_mes, qzeros, scales, Y, ldy, M, N, K,
-                                 group_size, 8, N / 2);
-  if (st != MES_OK) return st < 0 ? MES_OK : st;
-  if (!aligned16(X) || !aligned16(Y) || !aligned16(qweight_mes)) return MES_ERR_ALIGN;
-  return dispatch_gemm<kEpiSilu>(X, ldx, qweight_mes, qzeros, scales, nullptr, Y, ldy, M, N, K,
-                                 (cudaStream_t)stream);
+  return mes_awq_gemm_ws(kEpiSilu, X, ldx, qweight_mes, qzeros, scales, nullptr, Y, ldy, M, N, K,
+                         group_size, nullptr, 0, stream);
 }

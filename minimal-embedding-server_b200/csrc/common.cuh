@@ -68,20 +68,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait on phase `parity` of `bar`.  Returns false when the CTA-wide abort flag is
 // raised (by this or another role) or when the wait exceeds kWaitLimitNs; in the latter
 // case the flag is raised and `code` is recorded in `*err`.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity,
+                                                volatile int* abort_flag, int* err, int code,
+                                                uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
     if (n & 63) continue;  // the abort flag and the clock are checked every 64 polls
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicCAS(err, 0, code);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          volatile int* abort_flag, int* err, int code) {
+  return mbar_wait_limit(bar, parity, abort_flag, err, code, kWaitLimitNs);
 }
 
 // Warp-wide bounded wait: every lane waits, then the warp reconverges and agrees on the

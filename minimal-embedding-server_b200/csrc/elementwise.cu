@@ -371,6 +371,20 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // =========================================================================================
 // C ABI
 // =========================================================================================
+// One thread waits on a fresh mbarrier of arrival count 1 through the library's bounded
+// wait (the one every pipeline role uses), arriving first when `arrive` is set.  Without the
+// arrival the phase never completes: after `limit_ns` the wait gives up, raises the CTA's
+// abort flag and records MES_ERR_TIMEOUT in the device error word, and the kernel returns.
+__global__ void wait_probe_kernel(uint64_t limit_ns, int arrive) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  mes::mbar_init(&bar, 1);
+  abort_flag = 0;
+  mes::fence_barrier_init();
+  if (arrive) mes::mbar_arrive(&bar);
+  mes::mbar_wait_limit(&bar, 0, &abort_flag, &g_err_elementwise, MES_ERR_TIMEOUT, limit_ns);
+}
+
 extern "C" int mes_elementwise_take_error(int* code) {
   int v = 0, zero = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_err_elementwise, sizeof(int));
@@ -531,4 +545,10 @@ extern "C" int mes_varlen_cu_seqlens(const void* workspace, int64_t T, int32_t* 
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(num_seqs, ws, 4, cudaMemcpyDeviceToDevice, s);
   return mes_host::from_cuda(e);
+}
+
+extern "C" int mes_wait_probe(int64_t limit_ns, int arrive, void* stream) {
+  if (limit_ns <= 0 || limit_ns > 100000000) return MES_ERR_INVALID;  // at most 100 ms
+  wait_probe_kernel<<<1, 1, 0, (cudaStream_t)stream>>>((uint64_t)limit_ns, arrive ? 1 : 0);
+  return mes_host::from_cuda(cudaGetLastError());
 }

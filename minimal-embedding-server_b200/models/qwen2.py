@@ -216,14 +216,27 @@ class DecoderModel(nn.Module):
             return int(env)
         return 16 if world_size <= 2 else 24 if world_size <= 4 else 32
 
+    # overlap_split value meaning "the host found no valid micro-batch boundary".
+    NO_SPLIT = -1
+
+    def _resolve_split(self, positions: torch.Tensor, overlap_split: int | None) -> int | None:
+        """The micro-batch boundary to use, or None for the unsplit forward.  A boundary the
+        caller worked out from the host copy of the batch (:meth:`overlap_split_host`; a
+        negative value when there is none) is taken as given - inside a CUDA-graph capture
+        no device read may happen; only ``None`` (not given) derives it from ``positions``
+        with one device synchronisation."""
+        if _tp_size() == 1:
+            return None
+        if overlap_split is None:
+            return self._overlap_split(positions)
+        return int(overlap_split) if overlap_split >= 0 else None
+
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor,
                 overlap_split: int | None = None) -> torch.Tensor:
         """``overlap_split``: at tp > 1, the micro-batch boundary (a sequence start) when the
-        caller knows it from the host copy of the batch (see :meth:`overlap_split_host`);
-        otherwise it is derived from ``positions`` with one device synchronisation."""
-        split = overlap_split if _tp_size() > 1 else None
-        if split is None:
-            split = self._overlap_split(positions)
+        caller knows it from the host copy of the batch (see :meth:`overlap_split_host`,
+        ``NO_SPLIT`` when there is none); ``None`` derives it from ``positions``."""
+        split = self._resolve_split(positions, overlap_split)
         if split is not None:
             return self._forward_overlapped(input_ids, positions, split)
         with batch_schedule(positions):
@@ -243,14 +256,16 @@ class DecoderModel(nn.Module):
         return self._nearest_middle(starts.numpy(), T)
 
     @classmethod
-    def overlap_split_host(cls, positions) -> int | None:
-        """:meth:`_overlap_split` from a host (numpy) copy of ``positions``."""
+    def overlap_split_host(cls, positions) -> int:
+        """:meth:`_overlap_split` from a host (numpy) copy of ``positions``; ``NO_SPLIT``
+        when the forward runs unsplit."""
         import numpy as np
         pos = np.asarray(positions)
         T = pos.shape[0]
         if _tp_size() == 1 or T < cls.overlap_min_tokens:
-            return None
-        return cls._nearest_middle(np.flatnonzero(pos[1:] != pos[:-1] + 1) + 1, T)
+            return cls.NO_SPLIT
+        split = cls._nearest_middle(np.flatnonzero(pos[1:] != pos[:-1] + 1) + 1, T)
+        return cls.NO_SPLIT if split is None else split
 
     @classmethod
     def _nearest_middle(cls, starts, T: int) -> int | None:

@@ -1,8 +1,9 @@
 """Write the golden fixtures of tests/golden/ by running the reference itself on CPU.
 
-Run in the development container (where /root/reference exists):
+Run where a checkout of the reference exists (its directory is given by ``--reference``
+or the environment variable ``MES_REFERENCE_DIR``):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference <reference checkout> [--only NAME ...]
 
 The reference's own Python model code (woodx9/minimal-embedding-server) runs on CPU with
 four harness-side adaptations and no change to its sources:
@@ -21,6 +22,20 @@ names) and are loaded through the reference's own ``ultils/loader.load_model``.
 Fixtures (all small): ``ref_ops.npz`` (per-op outputs), ``ref_qwen3_c1.npz`` (the 0.6B
 architecture, 28 layers, 4 x 128 tokens, fp32), ``ref_qwen2_small.npz`` (Qwen2-1.5B
 shapes, 2 layers, ragged batch), ``awq_pack_vllm.npz`` (vLLM 0.22.0 ``awq_pack``).
+
+Benchmark-configuration fixtures (``ref_awq_<config>.npz``): the seeded AWQ checkpoint of
+the configuration (codes and zero-points uniform in [0, 15], fp16 scales uniform in
+[0.002, 0.02], ``mes_b200.synthetic.awq_weights`` on the CPU generator, so any machine
+regenerates it bit for bit; checksums of its tensors are stored to prove that) is
+dequantised exactly to fp32 and loaded as the dense weights of the reference's model.
+Stored are the reference's last-token L2-normalised embeddings in fp32 (the parity
+target, the "fp32 dequantised reference") and in bf16 (the reference's deployment dtype,
+whose own distance from fp32 is the yardstick for ours), plus the oracle's fp32
+restatement on the same inputs.
+  * ``c2``: Qwen3-Embedding-0.6B, 28 layers, 20 x 1000 tokens;
+  * ``c4_slice``: Qwen3-Embedding-8B shapes, 2 layers, a 4096-token sequence plus
+    log-uniform [64, 4096] lengths (8192 tokens);
+  * ``c5``: Qwen2-1.5B, 28 layers, 64 sequences of uniform [16, 512] tokens.
 """
 from __future__ import annotations
 
@@ -38,7 +53,7 @@ import torch.nn.functional as F  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REFERENCE = "/root/reference"
+REFERENCE = None   # the reference checkout, from --reference / MES_REFERENCE_DIR
 
 
 def _stub_flash_attn():
@@ -62,6 +77,8 @@ def _stub_flash_attn():
 
 
 def _setup_reference():
+    if not REFERENCE or not os.path.isdir(REFERENCE):
+        raise SystemExit("give the reference checkout with --reference or MES_REFERENCE_DIR")
     _stub_flash_attn()
     sys.path.insert(0, REFERENCE)
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
@@ -212,20 +229,99 @@ def awq_pack_fixture():
     print("awq_pack_vllm.npz", packed.shape, packed.dtype)
 
 
+# Benchmark configurations of the AWQ parity fixtures: (architecture, overrides,
+# lengths, weight seed, batch seed, norm noise).
+def awq_configs():
+    from mes_b200 import synthetic
+    c4_lengths = [4096] + synthetic.lengths_log_uniform(4096, 64, 4096, seed=3)
+    return {
+        "c2": (synthetic.qwen3_0_6b, dict(max_position_embeddings=32768), [1000] * 20, 0, 1, 0.1),
+        "c4_slice": (synthetic.qwen3_8b, dict(num_hidden_layers=2, max_position_embeddings=32768),
+                     c4_lengths, 0, 1, 0.1),
+        "c5": (synthetic.qwen2_1_5b, dict(max_position_embeddings=32768),
+               synthetic.lengths_uniform(64, 16, 512, seed=1), 0, 1, 0.1),
+    }
+
+
+def weight_checksums(weights: dict) -> dict:
+    """Exact integer checksums of every AWQ tensor and the embedding table's bits: a
+    regenerated checkpoint matches the fixture's only if every sum matches."""
+    out = {}
+    for name in sorted(weights):
+        t = weights[name]
+        if t.dtype in (torch.float16, torch.bfloat16):
+            t = t.view(torch.int16)
+        out[name] = int(t.to(torch.int64).sum())
+    return out
+
+
+def awq_config_fixture(name):
+    from mes_b200 import synthetic
+    sys.path.insert(0, REPO)
+    from oracle import model as omodel
+    arch, over, lengths, wseed, bseed, noise = awq_configs()[name]
+    cfg = arch(**over)
+    weights = synthetic.awq_weights(cfg, seed=wseed, device="cpu", norm_noise=noise)
+    sums = weight_checksums(weights)
+    dense = omodel.awq_dense_weights(weights)
+    del weights
+    ids, pos, last = synthetic.packed_batch(lengths, cfg.vocab_size, seed=bseed)
+    qk = not synthetic.is_qwen2(cfg)
+    out = dict(lengths=np.asarray(lengths, dtype=np.int64), weight_seed=wseed, batch_seed=bseed,
+               norm_noise=noise, checksum_names=np.asarray(list(sums)),
+               checksum_values=np.asarray(list(sums.values()), dtype=np.int64))
+    out["emb_oracle_fp32"] = omodel.embed(cfg, dense, torch.from_numpy(ids), torch.from_numpy(pos),
+                                          torch.from_numpy(last), qk_norm=qk).numpy()
+    _fix_rmsnorm_alias()
+    m = _reference_model(cfg, dense, torch.float32)
+    out["emb_fp32"], _ = _embed(m, ids, pos, last, torch.float32)
+    del m
+    _restore_rmsnorm()
+    m = _reference_model(cfg, dense, torch.bfloat16)
+    out["emb_bf16"], _ = _embed(m, ids, pos, last, torch.bfloat16)
+    del m
+    path = os.path.join(HERE, f"ref_awq_{name}.npz")
+    np.savez_compressed(path, **out)
+    cos = lambda a, b: (a * b).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
+    print(path, "reference bf16 vs fp32 cosine min", cos(out["emb_bf16"], out["emb_fp32"]).min(),
+          "oracle vs reference fp32 min", cos(out["emb_oracle_fp32"], out["emb_fp32"]).min())
+
+
 def main():
+    import argparse
+    global REFERENCE
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("MES_REFERENCE_DIR"),
+                    help="directory of the reference checkout")
+    ap.add_argument("--only", nargs="*", default=None,
+                    help="fixtures to write (ops, c1, qwen2_small, awq_pack, c2, c4_slice, c5)")
+    args = ap.parse_args()
+    REFERENCE = args.reference
     sys.path.insert(0, REPO)
     import __graft_entry__
     __graft_entry__.load_package()
     from mes_b200 import synthetic
     _setup_reference()
     torch.set_num_threads(os.cpu_count() or 1)
-    awq_pack_fixture()
-    ops_fixture()
-    model_fixture("ref_qwen3_c1.npz", synthetic.qwen3_0_6b(max_position_embeddings=32768),
-                  [128, 128, 128, 128])
-    model_fixture("ref_qwen2_small.npz",
-                  synthetic.qwen2_1_5b(num_hidden_layers=2, max_position_embeddings=32768),
-                  [1, 17, 64, 200])
+    want = set(args.only) if args.only else None
+
+    def on(name):
+        return want is None or name in want
+
+    if on("awq_pack"):
+        awq_pack_fixture()
+    if on("ops"):
+        ops_fixture()
+    if on("c1"):
+        model_fixture("ref_qwen3_c1.npz", synthetic.qwen3_0_6b(max_position_embeddings=32768),
+                      [128, 128, 128, 128])
+    if on("qwen2_small"):
+        model_fixture("ref_qwen2_small.npz",
+                      synthetic.qwen2_1_5b(num_hidden_layers=2, max_position_embeddings=32768),
+                      [1, 17, 64, 200])
+    for name in awq_configs():
+        if on(name):
+            awq_config_fixture(name)
 
 
 if __name__ == "__main__":

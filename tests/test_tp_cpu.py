@@ -111,11 +111,12 @@ def test_overlap_split_is_a_sequence_start_near_the_middle(monkeypatch):
     monkeypatch.setattr(qwen2, "_tp_size", lambda: 2)
     pos = np.concatenate([np.arange(n) for n in (1000, 700, 1300, 1000, 1000)])
     assert qwen2.DecoderModel.overlap_split_host(pos) == 3000     # starts 1000, 1700, 3000, 4000
-    assert qwen2.DecoderModel.overlap_split_host(np.arange(5000)) is None       # one sequence
-    assert qwen2.DecoderModel.overlap_split_host(np.arange(100)) is None        # below the threshold
+    NO = qwen2.DecoderModel.NO_SPLIT
+    assert qwen2.DecoderModel.overlap_split_host(np.arange(5000)) == NO         # one sequence
+    assert qwen2.DecoderModel.overlap_split_host(np.arange(100)) == NO          # below the threshold
     # A micro-batch of 256 tokens or fewer is never cut off (its GEMMs would split K).
     edge = np.concatenate([np.arange(4800), np.arange(200)])
-    assert qwen2.DecoderModel.overlap_split_host(edge) is None
+    assert qwen2.DecoderModel.overlap_split_host(edge) == NO
     edge = np.concatenate([np.arange(200), np.arange(2000), np.arange(2800)])
     assert qwen2.DecoderModel.overlap_split_host(edge) == 2200
     # The model's own path (positions as a torch tensor) applies the same rule.
@@ -124,6 +125,31 @@ def test_overlap_split_is_a_sequence_start_near_the_middle(monkeypatch):
     assert D._overlap_split(D, torch.from_numpy(pos)) == 3000
     assert D._overlap_split(D, torch.from_numpy(np.concatenate([np.arange(4800), np.arange(200)]))) is None
     monkeypatch.setattr(qwen2, "_tp_size", lambda: 1)
-    assert qwen2.DecoderModel.overlap_split_host(pos) is None                  # tp == 1
+    assert qwen2.DecoderModel.overlap_split_host(pos) == NO                    # tp == 1
     assert qwen2.DecoderModel.overlap_reserved_sms(2) == 16
     assert qwen2.DecoderModel.overlap_reserved_sms(8) == 32
+
+
+def test_host_split_is_used_as_given(monkeypatch):
+    """A boundary the host worked out - including "none" for a 4096+-token single sequence -
+    is used without the device read (which a CUDA-graph capture forbids); only an absent
+    one is derived from the positions."""
+    import numpy as np
+    import torch
+    from mes_b200.models import qwen2
+    monkeypatch.setattr(qwen2, "_tp_size", lambda: 2)
+    D = qwen2.DecoderModel
+    one_seq = np.arange(8192)
+    host = D.overlap_split_host(one_seq)
+    assert host == D.NO_SPLIT
+
+    def no_device_read(*args):
+        raise AssertionError("device read of the split")
+    monkeypatch.setattr(D, "_overlap_split", no_device_read)
+    pos_t = torch.from_numpy(one_seq)
+    assert D._resolve_split(D, pos_t, host) is None
+    assert D._resolve_split(D, pos_t, 3000) == 3000
+    with pytest.raises(AssertionError):
+        D._resolve_split(D, pos_t, None)
+    monkeypatch.setattr(qwen2, "_tp_size", lambda: 1)
+    assert D._resolve_split(D, pos_t, None) is None
