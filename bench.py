@@ -55,10 +55,17 @@ def parse_args():
     ap.add_argument("--impl", choices=["mes", "reference"], default="mes")
     ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "ew"], default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the varying-batch e2e stream and the last-rows variant")
+    ap.add_argument("--parallel", choices=["tp", "dp"], default="tp",
+                    help="tp: one batch sharded over the ranks (tensor parallel, the "
+                         "reference's layout); dp: every rank a full replica on its own batch")
     ap.add_argument("--gemm-shapes", default="qkv,o,gate_up,down",
                     help="c3 only: comma list of projection shapes to time")
     ap.add_argument("--gemm-m", default="16,256,2048,20000,120000",
                     help="c3 only: comma list of token counts M")
+    ap.add_argument("--gemm-epilogue", choices=["bf16", "silu", "residual"], default="bf16",
+                    help="c3 only: GEMM epilogue")
     return ap.parse_args()
 
 
@@ -246,8 +253,9 @@ def run_mes(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
+    dp = args.parallel == "dp"
+    import datetime
+    if world > 1 and not dp:
         from mes_b200.core.gpu_worker import tp_nccl_environment
         tp_nccl_environment()
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
@@ -256,7 +264,11 @@ def run_mes(args):
     ids, pos, last = synthetic.packed_batch(lengths, cfg.vocab_size, seed=1)
     T = len(ids)
 
+    # Data-parallel replicas: the model is built before the process group exists, so it
+    # is not sharded; the group only carries the barriers and the max over ranks.
     worker = GPUWorker(MESConfig(model_config=cfg), device=dev)
+    if world > 1 and dp:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     # Seeded synthetic weights generated on the device (same seed on every rank; each
     # rank's loaders keep only its shard).
     weights = synthetic.awq_weights(cfg, seed=0, device=dev)
@@ -289,6 +301,7 @@ def run_mes(args):
             d[2] += f
         return by_shape
 
+    from mes_b200.models.qwen2 import DecoderModel
     layout = worker.layout(pos, exact=True)   # the batch's own layout: no padding
     split = layout.split
 
@@ -313,7 +326,7 @@ def run_mes(args):
         # captured with it, so every replay times those launches on their stream.
         _C.gemm_events, _C.gemm_event_kinds = [], {probe_key[0]}
         launches0 = _C.launch_count
-        graph, ids_s, pos_s, _ = worker.capture(layout, ids, pos)
+        graph, ids_s, pos_s, _, _ = worker.capture(layout, ids, pos)
         launches = (_C.launch_count - launches0) // 2   # capture() runs the forward twice
         captured = _C.gemm_events[len(_C.gemm_events) // 2:]
         _C.gemm_events, _C.gemm_event_kinds = None, None
@@ -337,7 +350,9 @@ def run_mes(args):
         del graph
 
         # ---- end-to-end through the public API (e2e) --------------------------------
-        for _ in range(2):
+        # Warm-up: the batch's first occurrences replay its token bucket's graph; from the
+        # `exact_after`-th on, a graph of its exact layout (no padding).
+        for _ in range(worker.exact_after + 1):
             worker.embed(ids, pos, last)
         barrier()
         t0 = time.perf_counter()
@@ -351,8 +366,15 @@ def run_mes(args):
 
         # ---- e2e over a stream of batches of varying size (the server's case) ---------
         varying = None
-        if args.workload == "c2":
-            varying = run_varying_stream(worker, cfg, barrier, max_over_ranks)
+        if args.workload == "c2" and not args.no_extras:
+            varying = run_varying_stream(worker, cfg, barrier, max_over_ranks,
+                                         replicas=world if dp else 1)
+
+        # ---- flagged variant: the last layer on the pooled rows only ----------------
+        last_rows = None
+        if split == DecoderModel.NO_SPLIT and not args.no_extras:
+            last_rows = run_last_rows(worker, ids, pos, last, args, barrier, max_over_ranks,
+                                      replicas=world if dp else 1)
 
     err = _C.take_device_error()
     if err:
@@ -365,7 +387,8 @@ def run_mes(args):
     kind, gm, gn, gk = top_key
     result = None
     if rank == 0:
-        value = T * args.steps / dt
+        replicas = world if dp else 1     # each dp rank processes its own batch
+        value = replicas * T * args.steps / dt
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             cpu = cpu_baseline_entry(cfg, lengths, os.cpu_count() or 1)
@@ -373,15 +396,16 @@ def run_mes(args):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dt / args.steps * 1000, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "weak" if dp else "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded AWQ weights and token ids)",
-            "config": {"workload": desc, "tokens": T, "sequences": len(lengths),
-                       "parallelism": f"tp{world}",
+            "config": {"workload": desc, "tokens": T * replicas, "sequences": len(lengths) * replicas,
+                       "parallelism": f"dp{world}" if dp else f"tp{world}",
                        "l2": "inputs larger than L2 (weights + activations > 126 MB per step)"},
-            "e2e": {"value": T * args.steps / e2e_dt, "unit": UNIT,
+            "e2e": {"value": replicas * T * args.steps / e2e_dt, "unit": UNIT,
                     "h2d_bytes_per_step": int(ids.nbytes + pos.nbytes + last.nbytes),
                     "d2h_bytes_per_step": int(out.numel() * 4)},
             "e2e_varying": varying,
+            "last_rows_only": last_rows,
             "gpu_launches": launches * args.steps,
             "cuda_graph": True,
             "roofline": {"kernel": f"awq_gemm ({kind} epilogue) M={gm} N={gn} K={gk}",
@@ -406,7 +430,52 @@ def run_mes(args):
     return result
 
 
-def run_varying_stream(worker, cfg, barrier, max_over_ranks, n_batches: int = 16):
+def run_last_rows(worker, ids, pos, last, args, barrier, max_over_ranks, replicas: int = 1):
+    """Flagged variant (not the headline): the same batch with the last layer's o_proj, MLP
+    and final norm computed for the B pooled rows only (``DecoderModel.forward_last_rows``;
+    the embeddings are unchanged).  ``value``: CUDA-graph replays with the batch resident,
+    CUDA events; ``e2e``: ``GPUWorker.embed`` in last-rows mode with host buffers."""
+    import time as _time
+    import torch
+    T = len(ids)
+    lay = worker.layout(pos, exact=True)
+    n_rows = -(-len(last) // 16) * 16
+    graph, _, _, rows_s, _ = worker.capture(lay, ids, pos, n_rows)
+    rows = torch.zeros(n_rows, dtype=torch.int64)
+    rows[:len(last)] = torch.from_numpy(last)
+    rows_s.copy_(rows)
+    for _ in range(2):
+        graph.replay()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record()
+    barrier()
+    dt = max_over_ranks(e0.elapsed_time(e1) / 1000.0)
+    del graph
+    worker.last_rows_only = True
+    try:
+        for _ in range(3):
+            worker.embed(ids, pos, last)
+        barrier()
+        t0 = _time.perf_counter()
+        for _ in range(args.steps):
+            worker.embed(ids, pos, last)
+        barrier()
+        e2e_dt = max_over_ranks(_time.perf_counter() - t0)
+    finally:
+        worker.last_rows_only = False
+    return {"value": replicas * T * args.steps / dt, "unit": UNIT,
+            "ms_per_step": dt / args.steps * 1000,
+            "e2e": {"value": replicas * T * args.steps / e2e_dt, "unit": UNIT},
+            "flag": "last layer's o_proj, MLP and final norm on the pooled rows only "
+                    "(same embeddings; not the headline number)"}
+
+
+def run_varying_stream(worker, cfg, barrier, max_over_ranks, replicas: int = 1,
+                       n_batches: int = 16):
     """``GPUWorker.embed`` over a seeded stream of batches of 20 sequences with lengths
     uniform in [500, 1500] (10-30 k tokens per batch, a different total each time), as the
     engine's batcher produces them.  The first pass includes the CUDA-graph captures of the
@@ -428,7 +497,7 @@ def run_varying_stream(worker, cfg, barrier, max_over_ranks, n_batches: int = 16
             worker.embed(ids, pos, last)
         barrier()
         dt = max_over_ranks(_time.perf_counter() - t0)
-        out[name] = {"value": tokens / dt, "captures": worker.captures - c0}
+        out[name] = {"value": replicas * tokens / dt, "captures": worker.captures - c0}
     return {"value": out["steady"]["value"], "unit": UNIT, "batches": n_batches,
             "tokens": tokens, "tokens_per_batch": [min(len(b[0]) for b in batches),
                                                    max(len(b[0]) for b in batches)],
@@ -469,10 +538,23 @@ def cold_launch_time(fn, args, dev) -> float:
     return statistics.median(times)
 
 
+GEMM_SHAPES = {
+    # Qwen3-Embedding-4B projections (the GEMM microbenchmark's shapes), K x N
+    "qkv": (2560, 6144), "o": (4096, 2560), "gate_up": (2560, 19456), "down": (9728, 2560),
+    # Qwen3-Embedding-0.6B and -8B projections (the forward's GEMMs)
+    "qkv_0.6b": (1024, 4096), "o_0.6b": (2048, 1024), "gate_up_0.6b": (1024, 6144),
+    "down_0.6b": (3072, 1024),
+    "qkv_8b": (4096, 6144), "o_8b": (4096, 4096), "gate_up_8b": (4096, 24576),
+    "down_8b": (12288, 4096),
+}
+
+
 def run_gemm_micro(args):
-    """AWQ W4A16 GEMM microbenchmark on the Qwen3-Embedding-4B projection shapes (one JSON
-    line per shape and M).  Each launch is timed alone with CUDA events and a cold L2
-    (``cold_launch_time``); the bound is min(tensor peak, arithmetic intensity x HBM)."""
+    """AWQ W4A16 GEMM microbenchmark (one JSON line per shape and M), by default on the
+    Qwen3-Embedding-4B projection shapes with the bf16 epilogue.  Each launch is timed
+    alone with CUDA events and a cold L2 (``cold_launch_time``); the bound is
+    min(tensor peak, arithmetic intensity x HBM).  For M > 256 a launch is the whole
+    library call: the dequantisation of the weight panel and the tensor-core GEMM."""
     import torch
     import __graft_entry__
     __graft_entry__.build()
@@ -480,25 +562,39 @@ def run_gemm_micro(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     peak_burst, _, hbm, peak_kind = peaks()
-    shapes = {"qkv": (2560, 6144), "o": (4096, 2560), "gate_up": (2560, 19456), "down": (9728, 2560)}
     gen = torch.Generator(device=dev).manual_seed(0)
+    epi = args.gemm_epilogue
     for name in args.gemm_shapes.split(","):
-        K, N = shapes[name]
+        K, N = GEMM_SHAPES[name]
         qw, qz, sc = synthetic.random_awq(K, N, gen, dev)
+        if epi == "silu":
+            qw, qz, sc = _C.interleave_gate_up(qw, qz, sc.view(torch.int16))
+            sc = sc.view(torch.float16)
         qwm, sc16 = _C.awq_repack(qw), sc.view(torch.int16)
         for M in (int(m) for m in args.gemm_m.split(",")):
             x = torch.randn(M, K, generator=gen, device=dev).to(torch.bfloat16)
-            y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
-            t = cold_launch_time(lambda: _C.awq_gemm(x, qwm, qz, sc16, None, y), args, dev)
+            if epi == "silu":
+                y = torch.empty(M, N // 2, dtype=torch.bfloat16, device=dev)
+                fn = lambda: _C.awq_gemm_silu(x, qwm, qz, sc16, y)
+            elif epi == "residual":
+                y = torch.zeros(M, N, dtype=torch.float32, device=dev)
+                fn = lambda: _C.awq_gemm_residual(x, qwm, qz, sc16, y)
+            else:
+                y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+                fn = lambda: _C.awq_gemm(x, qwm, qz, sc16, None, y)
+            t = cold_launch_time(fn, args, dev)
             flops = 2.0 * M * N * K
-            nbytes = K * N / 2 + (K // 128) * N * 2.5 + 2 * M * K + 2 * M * N
+            out_bytes = {"silu": M * N, "residual": 8 * M * N}.get(epi, 2 * M * N)
+            nbytes = K * N / 2 + (K // 128) * N * 2.5 + 2 * M * K + out_bytes
             bound_tflops = min(peak_burst, flops / nbytes * hbm * 1e9 / 1e12)
             tf = flops / t / 1e12
             print(json.dumps({
-                "metric": "AWQ W4A16 GEMM TFLOP/s", "shape": name, "M": M, "N": N, "K": K,
-                "value": tf, "unit": "TFLOP/s", "us": t * 1e6, "steps": args.steps,
-                "frac_of_tensor_peak": tf / peak_burst, "bound": "tensor" if bound_tflops >= peak_burst else "hbm",
+                "metric": "AWQ W4A16 GEMM TFLOP/s", "shape": name, "epilogue": epi, "M": M,
+                "N": N, "K": K, "value": tf, "unit": "TFLOP/s", "us": t * 1e6,
+                "steps": args.steps, "frac_of_tensor_peak": tf / peak_burst,
+                "bound": "tensor" if bound_tflops >= peak_burst else "hbm",
                 "frac_of_bound": tf / bound_tflops, "peak_kind": f"{peak_kind} bf16 burst",
+                "weight_panel": bool(_C.lib().mes_awq_gemm_workspace_size(M, N, K)),
                 "l2": COLD_L2}), flush=True)
             del x, y
 

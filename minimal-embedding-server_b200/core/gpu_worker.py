@@ -21,13 +21,22 @@ The engine's batcher packs whole requests up to a token budget
 (``core/tokenizer_manager.py:98-139``), so the token count T varies from batch to batch.
 A graph is therefore keyed on a *bucketed* layout: the batch (each tensor-parallel
 micro-batch separately) is padded up to the next bucket size (multiples of 256 tokens up
-to 4096, of 1024 up to 32768, of 4096 beyond) with dummy sequences of at most 128 tokens,
-whose rows are never pooled and cost almost no attention.  A new T then reuses the graph of
-its bucket; a T that repeats gets a graph of its exact layout on its second occurrence (no
-padding at all).  Every row of a real token is computed exactly as in the unpadded forward
-(row results of every kernel are independent of the other rows of batches of more than 256
-tokens, and the dummy sequences attend only to themselves).  All graphs share one memory
-pool, so holding several costs the memory of the largest, not their sum.
+to 32768, of 2048 up to 131072, of 8192 beyond: about 1% padding at 20 k tokens) with dummy
+sequences of at most 128 tokens, whose rows are never pooled and cost almost no attention.
+A new T then reuses the graph of its bucket, and a stream of varying batches settles on a
+fixed set of graphs.  A layout that keeps repeating exactly (``exact_after`` times) gets a
+graph of its own, without padding.  A capture costs about three forwards, so this pays
+only for shapes that recur many times.  Every row of a real token is computed exactly as
+in the unpadded forward (row results of every kernel are independent of the other rows of
+batches of more than 256 tokens, and the dummy sequences attend only to themselves).  All
+graphs share one memory pool, so holding several costs the memory of the largest, not
+their sum.
+
+Last rows only (``last_rows_only=True`` or ``MES_LAST_ROWS_ONLY=1``; off by default).  The
+post-process pools one token per sequence, so ``embed`` can run the last layer's o_proj, MLP
+and final norm on those B rows alone (``DecoderModel.forward_last_rows``); the embeddings
+are the same, and ``_inference`` (all rows) is unaffected.  The graph of such a batch also
+holds the row indices (padded to a multiple of 16 with row 0; the extra rows are dropped).
 """
 from __future__ import annotations
 
@@ -58,8 +67,9 @@ def tp_nccl_environment(world_size: int | None = None) -> None:
 
 def token_bucket(n: int) -> int:
     """Padded token count of a (micro-)batch of ``n`` tokens: the next multiple of 256 up
-    to 4096, of 1024 up to 32768, of 4096 beyond (at most ~6% padding, ~3% typical)."""
-    step = 256 if n <= 4096 else 1024 if n <= 32768 else 4096
+    to 32768, of 2048 up to 131072, of 8192 beyond (at most 256 / n, 2048 / n or
+    8192 / n padding: ~1.3% at 20 k tokens)."""
+    step = 256 if n <= 32768 else 2048 if n <= 131072 else 8192
     return max(step, -(-n // step) * step)
 
 
@@ -119,9 +129,12 @@ class GPUWorker:
             with torch.device(self.device):
                 model = get_model_class(mes_config.model_config)(mes_config)
         self.model = model.eval()
+        self.tp_size = getattr(self.model, "tp_size", self.world_size)
+        self.last_rows_only = os.environ.get("MES_LAST_ROWS_ONLY", "0") == "1"
         self.use_cuda_graphs = os.environ.get("MES_CUDA_GRAPHS", "1") != "0"
-        self.max_graphs = 32         # bucketed layouts kept (least recently used dropped)
-        self.max_exact_graphs = 4    # exact layouts of repeated token counts kept
+        self.max_graphs = 128        # bucketed layouts kept (least recently used dropped)
+        self.max_exact_graphs = 8    # exact layouts of repeated token counts kept
+        self.exact_after = 8         # occurrences of an exact layout before it gets a graph
         self._graphs: collections.OrderedDict = collections.OrderedDict()
         self._exact: collections.OrderedDict = collections.OrderedDict()
         self._seen: collections.Counter = collections.Counter()
@@ -141,7 +154,7 @@ class GPUWorker:
         ``exact``, each micro-batch padded to its token bucket."""
         pos = np.asarray(positions)
         T = int(pos.shape[0])
-        split = DecoderModel.overlap_split_host(pos)
+        split = DecoderModel.overlap_split_host(pos, self.tp_size)
         if split == DecoderModel.NO_SPLIT:
             spans = [(0, T)]
         else:
@@ -155,60 +168,74 @@ class GPUWorker:
         return Layout(parts, dev_split)
 
     def _graph_layout(self, positions) -> Layout:
-        """Layout to run a host batch with: exact when its graph exists or its token layout
-        was seen before (it repeats), else bucketed."""
+        """Layout to run a host batch with: exact when its graph exists, its layout needs no
+        padding, or it has now occurred ``exact_after`` times; else bucketed."""
         exact = self.layout(positions, exact=True)
-        if exact.key in self._exact:
+        if any(k[0] == exact.key for k in self._exact):
             return exact
+        bucket = self.layout(positions)
+        if not bucket.padded:
+            return exact
+        if len(self._seen) > 4096:       # forget old shapes; the counts only pick exact graphs
+            self._seen.clear()
         self._seen[exact.key] += 1
-        if self._seen[exact.key] >= 2 or not self.layout(positions).padded:
-            return exact
-        return self.layout(positions)
+        return exact if self._seen[exact.key] >= self.exact_after else bucket
 
-    def _graph_for(self, lay: Layout, ids, pos):
-        """The captured forward of layout ``lay`` (captured on first use); None if capture
-        failed (that layout then runs eagerly)."""
+    def _graph_for(self, lay: Layout, ids, pos, n_rows: int = 0):
+        """The captured forward of layout ``lay`` (with ``n_rows`` last rows, see
+        :meth:`capture`), captured on first use; None if capture failed (that layout then
+        runs eagerly)."""
         cache, limit = (self._graphs, self.max_graphs) if lay.padded else (self._exact, self.max_exact_graphs)
-        g = cache.get(lay.key)
+        key = (lay.key, n_rows)
+        g = cache.get(key)
         if g is not None:
-            cache.move_to_end(lay.key)
+            cache.move_to_end(key)
             return g
         try:
-            g = self.capture(lay, ids, pos)
+            g = self.capture(lay, ids, pos, n_rows)
         except Exception as exc:   # an unsupported capture runs eagerly from now on
             warnings.warn(f"CUDA-graph capture of a {lay.total}-token batch failed ({exc!r}); "
                           "batches of this layout run eagerly", RuntimeWarning, stacklevel=2)
-            self._no_graph.add(lay.key)
+            self._no_graph.add(key)
             return None
-        cache[lay.key] = g
+        cache[key] = g
         while len(cache) > limit:
             cache.popitem(last=False)
         return g
 
     @torch.no_grad()
-    def capture(self, lay: Layout, input_ids, positions):
+    def capture(self, lay: Layout, input_ids, positions, n_rows: int = 0):
         """Capture one forward of layout ``lay`` into a CUDA graph (memory from the worker's
-        shared graph pool).  Returns ``(graph, ids, positions, out)``: the static device
-        input buffers to fill (padded) before ``graph.replay()`` and the ``[lay.total, H]``
-        output it writes.  ``input_ids`` / ``positions``: a host batch of that layout (not
-        yet padded), run once eagerly first."""
+        shared graph pool).  Returns ``(graph, ids, positions, rows, out)``: the static
+        device input buffers to fill (padded) before ``graph.replay()`` and the output it
+        writes - ``[lay.total, H]``, or with ``n_rows`` > 0 the final states ``[n_rows, H]``
+        of the rows listed in ``rows`` (int64 [n_rows]; :meth:`DecoderModel.forward_last_rows`).
+        ``input_ids`` / ``positions``: a host batch of that layout (not yet padded), run
+        once eagerly first."""
         ids_h, pos_h = lay.pad(np.asarray(input_ids), np.asarray(positions))
         ids_s = torch.empty(lay.total, dtype=torch.int64, device=self.device)
         pos_s = torch.empty(lay.total, dtype=torch.int64, device=self.device)
+        rows_s = torch.zeros(n_rows, dtype=torch.int64, device=self.device) if n_rows else None
         ids_s.copy_(self._to_device(ids_h))
         pos_s.copy_(self._to_device(pos_h))
+
+        def run():
+            if n_rows:
+                return self.model.forward_last_rows(ids_s, pos_s, rows_s)
+            return self.model(ids_s, pos_s, overlap_split=lay.split)
+
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(side):
-            self.model(ids_s, pos_s, overlap_split=lay.split)
+            run()
         torch.cuda.current_stream(self.device).wait_stream(side)
         if self._pool is None:
             self._pool = torch.cuda.graph_pool_handle()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, pool=self._pool):
-            out = self.model(ids_s, pos_s, overlap_split=lay.split)
+            out = run()
         self.captures += 1
-        return graph, ids_s, pos_s, out
+        return graph, ids_s, pos_s, rows_s, out
 
     def release_graphs(self) -> None:
         """Drop every captured graph (required before the process group is destroyed when
@@ -218,26 +245,40 @@ class GPUWorker:
 
     # ---------------------------------------------------------------- forward
     @torch.no_grad()
-    def _forward(self, input_ids, positions):
-        """Forward of one batch: ``(hidden, layout)`` where ``hidden`` holds the model
-        output in the device layout (``layout.rows`` maps host token indices to its rows;
-        ``layout`` is None for an unpadded eager forward)."""
+    def _forward(self, input_ids, positions, last_token_indices=None):
+        """Forward of one batch: ``(hidden, layout)``.  ``hidden`` holds the model output in
+        the device layout (``layout.rows`` maps host token indices to its rows; ``layout``
+        is None for an unpadded eager forward) - or, when ``last_token_indices`` is given
+        and the last-rows forward applies, the final states of exactly those tokens, in
+        their order (``layout`` is then the string "rows")."""
         host = not (isinstance(positions, torch.Tensor) and positions.is_cuda)
+        rows_mode = last_token_indices is not None
         if self.use_cuda_graphs and host:
             ids_h = np.asarray(input_ids.numpy() if isinstance(input_ids, torch.Tensor) else input_ids)
             pos_h = np.asarray(positions.numpy() if isinstance(positions, torch.Tensor) else positions)
             lay = self._graph_layout(pos_h)
-            if lay.key not in self._no_graph:
-                g = self._graph_for(lay, ids_h, pos_h)
+            rows_mode = rows_mode and lay.split == DecoderModel.NO_SPLIT
+            n_rows = -(-len(last_token_indices) // 16) * 16 if rows_mode else 0
+            if (lay.key, n_rows) not in self._no_graph:
+                g = self._graph_for(lay, ids_h, pos_h, n_rows)
                 if g is not None:
-                    graph, ids_s, pos_s, out = g
+                    graph, ids_s, pos_s, rows_s, out = g
                     ids_p, pos_p = lay.pad(ids_h, pos_h)
                     ids_s.copy_(self._to_device(ids_p), non_blocking=True)
                     pos_s.copy_(self._to_device(pos_p), non_blocking=True)
+                    if rows_mode:
+                        rows = np.zeros(n_rows, dtype=np.int64)
+                        rows[:len(last_token_indices)] = lay.rows(last_token_indices)
+                        rows_s.copy_(self._to_device(rows), non_blocking=True)
                     graph.replay()
+                    if rows_mode:
+                        return out[:len(last_token_indices)], "rows"
                     return out, lay
         input_ids = self._to_device(input_ids).to(torch.int64)
         positions = self._to_device(positions).to(torch.int64)
+        if rows_mode and (self.tp_size == 1 or self.model.model._overlap_split(positions) is None):
+            rows = self._to_device(torch.as_tensor(np.asarray(last_token_indices), dtype=torch.int64))
+            return self.model.forward_last_rows(input_ids, positions, rows), "rows"
         return self.model(input_ids=input_ids, positions=positions), None
 
     @torch.no_grad()
@@ -263,7 +304,14 @@ class GPUWorker:
         return host
 
     def embed(self, input_ids, positions, last_token_indices) -> torch.Tensor:
-        out, lay = self._forward(input_ids, positions)
+        """fp32 ``[B, H]`` embeddings: ``_inference`` + ``postprocess`` (the engine's call
+        per batch)."""
+        if self.last_rows_only:
+            out, lay = self._forward(input_ids, positions, last_token_indices)
+            if lay == "rows":
+                return self.postprocess(out, np.arange(out.shape[0]))
+        else:
+            out, lay = self._forward(input_ids, positions)
         if lay is not None and lay.padded:
             last_token_indices = lay.rows(last_token_indices)
         return self.postprocess(out, last_token_indices)

@@ -57,7 +57,8 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
   uint64_t* s_free = s_full + 2;                  // [2]
   uint64_t* p_full = s_free + 2;
   uint64_t* pv_done = p_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
+  uint64_t* drain = pv_done + 1;                  // abort path: issued MMAs completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = mes::warp_id(), lane = mes::lane_id();
@@ -78,6 +79,7 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
     }
     mes::mbar_init(p_full, 4);
     mes::mbar_init(pv_done, 1);
+    mes::mbar_init(drain, 1);
     *abort_flag = 0;
     mes::fence_barrier_init();
   }
@@ -95,7 +97,7 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
   if (warp == 0) {
     // ------------------------------------ TMA ----------------------------------------
     if (lane == 0) {
-      int n_item = 0, kvit = 0;
+      int n_item = 0, kvit = 0, q_issued = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < num_work && ok; w += gridDim.x, ++n_item) {
         const int2 it = items[w / Hq];
@@ -106,6 +108,7 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
           ok = false;
           break;
         }
+        ++q_issued;
         mes::mbar_arrive_expect_tx(q_full, kQBytes);
         mes::tma_load_2d(qs, &map_qkv, q_full, h * kD, q0);
         mes::tma_load_2d(qs + kQBytes / 2, &map_qkv, q_full, h * kD + 64, q0);
@@ -129,9 +132,18 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
         }
       }
       if (!ok) {
-        // Give copies already in flight time to land before the CTA exits.
-        const uint64_t t = mes::globaltimer_ns();
-        while (mes::globaltimer_ns() - t < 1000000ull) {
+        // Let the copies already issued land before the CTA exits: the last Q tile and the
+        // last kKVStages K and V tiles (bounded, one deadline for all).
+        const uint64_t t0 = mes::globaltimer_ns();
+        auto landed = [&](uint64_t* bar, int n, int stages) {
+          while (!mes::mbar_try_wait(&bar[n % stages], (n / stages) & 1) &&
+                 mes::globaltimer_ns() - t0 < mes::kWaitLimitNs) {
+          }
+        };
+        if (q_issued > 0) landed(q_full, q_issued - 1, 1);
+        for (int i = kvit - kKVStages < 0 ? 0 : kvit - kKVStages; i < kvit; ++i) {
+          landed(k_full, i, kKVStages);
+          landed(v_full, i, kKVStages);
         }
       }
     }
@@ -185,8 +197,10 @@ varlen_attention_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat
         it += nt;
       }
       if (!ok) {
-        const uint64_t t = mes::globaltimer_ns();
-        while (mes::globaltimer_ns() - t < 1000000ull) {
+        // Wait (bounded) until every MMA issued so far has completed.
+        mes::tc_commit(drain);
+        const uint64_t t0 = mes::globaltimer_ns();
+        while (!mes::mbar_try_wait(drain, 0) && mes::globaltimer_ns() - t0 < mes::kWaitLimitNs) {
         }
       }
     }
@@ -425,7 +439,8 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
   uint64_t* s_full = bars + 10;   // [2] per head of the pair
   uint64_t* p_full = bars + 12;   // [2]
   uint64_t* o_full = bars + 14;   // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* drain = bars + 16;    // abort path: issued MMAs completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = mes::warp_id(), lane = mes::lane_id();
@@ -447,6 +462,7 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
       mes::mbar_init(&p_full[b], 4);
       mes::mbar_init(&o_full[b], 1);
     }
+    mes::mbar_init(drain, 1);
     *abort_flag = 0;
     mes::fence_barrier_init();
   }
@@ -466,7 +482,7 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
    if (warp == 8) {
     // ------------------------------------ TMA ----------------------------------------
     if (lane == 0) {
-      int n_item = 0, kt = 0, vt = 0;
+      int n_item = 0, kt = 0, vt = 0, q_issued = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < num_work && ok; w = snake(++n_item, blockIdx.x, gridDim.x)) {
         const int2 it = items[w / npairs];
@@ -477,12 +493,13 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
           ok = false;
           break;
         }
+        ++q_issued;
         mes::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           mes::tma_load_2d(qs + c * (kQBytes / 2), &map_qkv, q_full, h0 * kD + c * 64, q0);
         const int kcol = (Hq + g) * kD, vcol = (Hq + Hkv + g) * kD;
-        for (int j = 0; j <= it.y; ++j, ++kt, ++vt) {
+        for (int j = 0; j <= it.y; ++j) {
           const int k0 = start + j * kTile;
           const int ks_ = kt % kKVStages, vs_ = vt % kKVStages;
           if (kt >= kKVStages &&
@@ -494,6 +511,7 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
           mes::mbar_arrive_expect_tx(&k_full[ks_], kKVBytes);
           mes::tma_load_2d(kd, &map_qkv, &k_full[ks_], kcol, k0);
           mes::tma_load_2d(kd + kKVBytes / 2, &map_qkv, &k_full[ks_], kcol + 64, k0);
+          ++kt;
           if (vt >= kKVStages &&
               !mes::mbar_wait(&v_empty[vs_], ((vt / kKVStages) & 1) ^ 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) {
             ok = false;
@@ -503,13 +521,21 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
           mes::mbar_arrive_expect_tx(&v_full[vs_], kKVBytes);
           mes::tma_load_2d(vd, &map_qkv, &v_full[vs_], vcol, k0);
           mes::tma_load_2d(vd + kKVBytes / 2, &map_qkv, &v_full[vs_], vcol + 64, k0);
+          ++vt;
         }
       }
       if (!ok) {
-        // Give copies already in flight time to land before the CTA exits.
-        const uint64_t t = mes::globaltimer_ns();
-        while (mes::globaltimer_ns() - t < 1000000ull) {
-        }
+        // Let the copies already issued land before the CTA exits: the last Q tiles and
+        // the last kKVStages K and V tiles (bounded, one deadline for all).
+        const uint64_t t0 = mes::globaltimer_ns();
+        auto landed = [&](uint64_t* bar, int n, int stages) {
+          while (!mes::mbar_try_wait(&bar[n % stages], (n / stages) & 1) &&
+                 mes::globaltimer_ns() - t0 < mes::kWaitLimitNs) {
+          }
+        };
+        if (q_issued > 0) landed(q_full, q_issued - 1, 1);
+        for (int i = kt - kKVStages < 0 ? 0 : kt - kKVStages; i < kt; ++i) landed(k_full, i, kKVStages);
+        for (int i = vt - kKVStages < 0 ? 0 : vt - kKVStages; i < vt; ++i) landed(v_full, i, kKVStages);
       }
     }
     __syncwarp();
@@ -584,8 +610,10 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
         }
       }
       if (!ok) {
-        const uint64_t t = mes::globaltimer_ns();
-        while (mes::globaltimer_ns() - t < 1000000ull) {
+        // Wait (bounded) until every MMA issued so far has completed.
+        mes::tc_commit(drain);
+        const uint64_t t0 = mes::globaltimer_ns();
+        while (!mes::mbar_try_wait(drain, 0) && mes::globaltimer_ns() - t0 < mes::kWaitLimitNs) {
         }
       }
     }

@@ -872,6 +872,25 @@ __device__ __forceinline__ void pair_tile(int tile, int num_n, int num_t, int ba
   t = r / width;
 }
 
+// Work item `i` of the pair kernels: the first `full` items are whole 256-token tiles in the
+// banded order; when the tiles leave a last round that would occupy at most half of the
+// pairs, the host makes the remaining tiles into two 128-token halves each (items `full`,
+// `full` + 1, ...), so the last round takes half a tile's time on twice as many pairs.
+struct PairItem {
+  int f;     // feature tile (256 features)
+  int t0;    // first token
+  int ntok;  // 256, or 128 for a half tile
+};
+__device__ __forceinline__ PairItem pair_item(int i, int full, int num_n, int num_t, int band) {
+  PairItem p;
+  const int tile = i < full ? i : full + ((i - full) >> 1);
+  int t;
+  pair_tile(tile, num_n, num_t, band, p.f, t);
+  p.ntok = i < full ? 256 : 128;
+  p.t0 = t * 256 + (i < full ? 0 : ((i - full) & 1) * 128);
+  return p;
+}
+
 template <int EPI, bool PANEL>
 __global__ void __launch_bounds__(QCfg<EPI, PANEL>::kThreads, 1)
 awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
@@ -880,7 +899,7 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
                      const __grid_constant__ CUtensorMap map_z,
                      const __grid_constant__ CUtensorMap map_y,
                      const __nv_bfloat16* __restrict__ bias, float* __restrict__ R, int64_t ldr,
-                     int M, int N, int K, int band) {
+                     int M, int N, int K, int band, int full, int num_items) {
   using C = QCfg<EPI, PANEL>;
   constexpr int SST = C::SST;
   constexpr uint32_t kTmemCols = 512;
@@ -908,7 +927,6 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
   const int nk = K / kBK;
   const int num_n = N / C::kTileN;
   const int num_t = (M + C::kTileT - 1) / C::kTileT;
-  const int num_tiles = num_n * num_t;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SST; ++s) {
@@ -950,11 +968,11 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
       const uint32_t full_x0 = mes::mapa_shared(mes::smem_u32(full_x), 0);
       int it = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-        int f, t;
-        pair_tile(tile, num_n, num_t, band, f, t);
-        const int n0 = f * C::kTileN + (int)rank * kBN;
-        const int t0 = t * C::kTileT + (int)rank * C::kHalfT;
+      for (int item = pair; item < num_items && ok; item += npairs) {
+        // A half tile uses the first 64 rows of each CTA's 128-row X box.
+        const PairItem pi = pair_item(item, full, num_n, num_t, band);
+        const int n0 = pi.f * C::kTileN + (int)rank * kBN;
+        const int t0 = pi.t0 + (int)rank * (pi.ntok / 2);
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % SST;
           if (it >= SST &&
@@ -994,11 +1012,13 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
   } else if (warp == 1) {
     // ------------------------------- MMA issuer (even CTA) ----------------------------
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = mes::idesc_bf16_f32(2 * kBN, C::kTileT, false);
+      constexpr uint32_t idesc_full = mes::idesc_bf16_f32(2 * kBN, C::kTileT, false);
+      constexpr uint32_t idesc_half = mes::idesc_bf16_f32(2 * kBN, C::kTileT / 2, false);
       const uint32_t xs_addr = mes::smem_u32(xs), as_addr = mes::smem_u32(as);
       int it = 0, lt = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++lt) {
+      for (int item = pair; item < num_items && ok; item += npairs, ++lt) {
+        const uint32_t idesc = item < full ? idesc_full : idesc_half;
         const int b = lt & 1;
         if (lt >= 2 &&
             !mes::mbar_wait(&acc_empty[b], ((lt >> 1) - 1) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT)) {
@@ -1044,7 +1064,7 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
       const uint32_t afull0 = mes::mapa_shared(mes::smem_u32(afull), 0);
       int it = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+      for (int item = pair; item < num_items && ok; item += npairs) {
         for (int kb = 0; kb < nk; ++kb, ++it) {
           if (it % C::SETS != set) continue;
           const int s = it % SST;
@@ -1093,19 +1113,18 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
     __nv_bfloat16* buf = outbuf + (warp - 2 - C::kDqWarps) * (C::kOutBuf / 2);
     bool stored = false;
     int lt = 0;
-    for (int tile = pair; tile < num_tiles; tile += npairs, ++lt) {
+    for (int item = pair; item < num_items; item += npairs, ++lt) {
       const int b = lt & 1;
-      int f, t;
-      pair_tile(tile, num_n, num_t, band, f, t);
-      const int n0 = f * C::kTileN + (int)rank * kBN;
-      const int t0 = t * C::kTileT;
+      const PairItem pi = pair_item(item, full, num_n, num_t, band);
+      const int n0 = pi.f * C::kTileN + (int)rank * kBN;
+      const int t0 = pi.t0;
       const int n = n0 + q * 32 + lane;
       if (!mes::mbar_wait_warp(&acc_full[b], (lt >> 1) & 1, abort_flag, &g_err_gemm, MES_ERR_TIMEOUT))
         break;
       mes::tc_fence_after();
       const float bv = bias ? __bfloat162float(bias[n]) : 0.f;
 #pragma unroll 1
-      for (int c0 = eh * C::kChunk; c0 < C::kTileT; c0 += 2 * C::kChunk) {
+      for (int c0 = eh * C::kChunk; c0 < pi.ntok; c0 += 2 * C::kChunk) {
         uint32_t v[C::kChunk];
         if constexpr (C::kChunk == 32) mes::tmem_ld32(tmem + lane_off + b * C::kTileT + c0, v);
         else mes::tmem_ld16(tmem + lane_off + b * C::kTileT + c0, v);
@@ -1433,7 +1452,11 @@ int launch_gemm_pair(const void* X, int64_t ldx, const void* w, const int32_t* q
   const int64_t num_n = N / C::kTileN;
   const int64_t tiles = num_n * ((M + C::kTileT - 1) / C::kTileT);
   const int64_t max_pairs = clusters < mes_host::persistent_ctas() / 2 ? clusters : mes_host::persistent_ctas() / 2;
-  const int64_t pairs = tiles < max_pairs ? tiles : max_pairs;
+  // A last round of at most half the pairs runs as half tiles on twice as many pairs.
+  const int64_t left = tiles % max_pairs;
+  const int64_t full = (left != 0 && 2 * left <= max_pairs) ? tiles - left : tiles;
+  const int64_t items = full + 2 * (tiles - full);
+  const int64_t pairs = items < max_pairs ? items : max_pairs;
   // Band of feature tiles walked at a time: the panel rows of a band (about 40 MB at most)
   // stay in L2 while the token tiles pass them.  The packed weights are 4x smaller and are
   // walked in one band.
@@ -1445,7 +1468,7 @@ int launch_gemm_pair(const void* X, int64_t ldx, const void* w, const int32_t* q
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mx, mw, ms, mz, my, (const __nv_bfloat16*)bias,
                          C::kResidual || C::kSilu ? (float*)Y : nullptr, ldy, (int)M, (int)N, (int)K,
-                         (int)band);
+                         (int)band, (int)full, (int)items);
   if (e != cudaSuccess) return MES_ERR_CUDA;
   return mes_host::from_cuda(cudaGetLastError());
 }

@@ -177,6 +177,24 @@ class DecoderLayer(nn.Module):
         delta = self.mlp.forward_residual(x, residual)
         return delta, residual
 
+    def forward_last_rows(self, positions: torch.Tensor, hidden_states: torch.Tensor | None,
+                          residual: torch.Tensor | None, rows: torch.Tensor):
+        """The block for the token rows ``rows`` (int64 [B]) only: attention still reads every
+        token's keys and values, but o_proj, the MLP and the residual updates run on the B
+        gathered rows.  Returns ``(pending_delta, residual_rows)`` like :meth:`forward`, for
+        the B rows."""
+        if residual is None:
+            residual = hidden_states
+            x = self.input_layernorm.residual_norm(residual)
+        else:
+            x = self.input_layernorm.residual_norm(residual, hidden_states)
+        attn = self.self_attn._attend(positions, x).index_select(0, rows)
+        res = residual.index_select(0, rows)
+        delta = self.self_attn.o_proj.forward_residual(attn, res)
+        x = self.post_attention_layernorm.residual_norm(res, delta)
+        delta = self.mlp.forward_residual(x, res)
+        return delta, res
+
 
 class Qwen2DecoderLayer(DecoderLayer):
 
@@ -197,6 +215,9 @@ class DecoderModel(nn.Module):
         self.layers = nn.ModuleList([self.layer_cls(mes_config)
                                      for _ in range(mc.num_hidden_layers)])
         self.norm = RMSNorm(mc.hidden_size, eps=mc.rms_norm_eps)
+        # The tensor-parallel group size the layers were sharded for (fixed here: a process
+        # group created later - e.g. for data-parallel replicas - does not shard the model).
+        self.tp_size = _tp_size()
 
     # Tensor parallelism: below this many tokens the batch is not split for overlap.
     overlap_min_tokens = int(os.environ.get("MES_TP_OVERLAP_MIN_TOKENS", "4096"))
@@ -225,7 +246,7 @@ class DecoderModel(nn.Module):
         negative value when there is none) is taken as given - inside a CUDA-graph capture
         no device read may happen; only ``None`` (not given) derives it from ``positions``
         with one device synchronisation."""
-        if _tp_size() == 1:
+        if self.tp_size == 1:
             return None
         if overlap_split is None:
             return self._overlap_split(positions)
@@ -246,23 +267,41 @@ class DecoderModel(nn.Module):
                 hidden_states, residual = layer(positions, hidden_states, residual)
             return self.norm.residual_norm(residual, hidden_states)
 
+    def forward_last_rows(self, input_ids: torch.Tensor, positions: torch.Tensor,
+                          rows: torch.Tensor) -> torch.Tensor:
+        """Final hidden states ``[B, H]`` of the token rows ``rows`` (int64 [B]) only - the
+        rows the embedding post-process pools (``core/gpu_worker.py:258``).  Every layer
+        but the last runs on all tokens; the last runs its o_proj, MLP and final norm on
+        the B rows (:meth:`DecoderLayer.forward_last_rows`).  Each returned row equals the
+        corresponding row of :meth:`forward`.  Unsplit forward only (tp == 1, or a batch
+        the tensor-parallel overlap does not split)."""
+        with batch_schedule(positions):
+            hidden_states = self.embed_tokens.forward_f32(input_ids)
+            residual = None
+            for layer in self.layers[:-1]:
+                hidden_states, residual = layer(positions, hidden_states, residual)
+            delta, res = self.layers[-1].forward_last_rows(positions, hidden_states, residual, rows)
+            return self.norm.residual_norm(res, delta)
+
     def _overlap_split(self, positions: torch.Tensor) -> int | None:
         """Token index of the sequence start nearest the middle of the batch, or None when
         the forward runs unsplit (tp == 1, a small batch, or a single sequence)."""
         T = positions.shape[0]
-        if _tp_size() == 1 or T < self.overlap_min_tokens:
+        if self.tp_size == 1 or T < self.overlap_min_tokens:
             return None
         starts = (torch.nonzero(positions[1:] != positions[:-1] + 1).flatten() + 1).cpu()
         return self._nearest_middle(starts.numpy(), T)
 
     @classmethod
-    def overlap_split_host(cls, positions) -> int:
-        """:meth:`_overlap_split` from a host (numpy) copy of ``positions``; ``NO_SPLIT``
-        when the forward runs unsplit."""
+    def overlap_split_host(cls, positions, tp_size: int | None = None) -> int:
+        """:meth:`_overlap_split` from a host (numpy) copy of ``positions`` for a model
+        sharded ``tp_size`` ways (default: the current process group's size);
+        ``NO_SPLIT`` when the forward runs unsplit."""
         import numpy as np
         pos = np.asarray(positions)
         T = pos.shape[0]
-        if _tp_size() == 1 or T < cls.overlap_min_tokens:
+        tp = _tp_size() if tp_size is None else tp_size
+        if tp == 1 or T < cls.overlap_min_tokens:
             return cls.NO_SPLIT
         split = cls._nearest_middle(np.flatnonzero(pos[1:] != pos[:-1] + 1) + 1, T)
         return cls.NO_SPLIT if split is None else split
@@ -287,7 +326,7 @@ class DecoderModel(nn.Module):
         T = positions.shape[0]
         parts = ((0, split), (split, T))
         pos = [positions[a:b] for a, b in parts]
-        _C.set_sm_reserve(self.overlap_reserved_sms(_tp_size()))
+        _C.set_sm_reserve(self.overlap_reserved_sms(self.tp_size))
         try:
             with batch_schedule(pos[0]), batch_schedule(pos[1]):
                 residual = self.embed_tokens.forward_f32(input_ids)
@@ -340,6 +379,10 @@ class CausalLMBase(nn.Module):
         self.mes_config = mes_config
         self.model = self.model_cls(mes_config)
 
+    @property
+    def tp_size(self) -> int:
+        return self.model.tp_size
+
     def process_weights_after_loading(self):
         """Repack every AWQ weight into the kernel layout (once, after loading)."""
         for m in self.modules():
@@ -349,6 +392,10 @@ class CausalLMBase(nn.Module):
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor,
                 overlap_split: int | None = None) -> torch.Tensor:
         return self.model(input_ids, positions, overlap_split)
+
+    def forward_last_rows(self, input_ids: torch.Tensor, positions: torch.Tensor,
+                          rows: torch.Tensor) -> torch.Tensor:
+        return self.model.forward_last_rows(input_ids, positions, rows)
 
 
 @register_model("Qwen2ForCausalLM")

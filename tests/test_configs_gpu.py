@@ -21,12 +21,20 @@ average at least as close to the fp32 reference as the reference's bf16 path
 0.9995); where the reference's bf16 path is within 0.9995 everywhere, ours must be too.
 """
 import os
+import sys
 
 import numpy as np
 import pytest
 import torch
 
-from mes_b200 import _C, synthetic
+# Spawned tensor-parallel ranks import this module by name before anything else has loaded
+# the package directory as ``mes_b200``.
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+import __graft_entry__  # noqa: E402
+
+__graft_entry__.load_package()
+
+from mes_b200 import _C, synthetic  # noqa: E402
 from mes_b200.core.gpu_worker import GPUWorker
 from mes_b200.schemas.config import MESConfig
 from mes_b200.ultils.loader import load_weights
@@ -112,6 +120,28 @@ def test_c5_qwen2_1_5b_tp1():
 
 
 # ------------------------------------------------------------- c5 at TP2 over NCCL
+def get_from_ranks(q, procs, timeout: float):
+    """The first result a rank puts on ``q``; fails as soon as a rank has exited with an
+    error instead of waiting for the whole timeout."""
+    import queue
+    import time
+    deadline = time.monotonic() + timeout
+    while time.monotonic() < deadline:
+        try:
+            return q.get(timeout=5)
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            if dead:
+                for p in procs:
+                    p.join(timeout=30)
+                    if p.is_alive():
+                        p.kill()
+                pytest.fail(f"a rank exited with {dead}")
+    for p in procs:
+        p.kill()
+    pytest.fail("no result from the ranks")
+
+
 def _tp2_rank(rank, port, q):
     import datetime
     import sys
@@ -159,7 +189,7 @@ def test_c5_qwen2_1_5b_tp2_one_kv_head_per_gpu():
     procs = [ctx.Process(target=_tp2_rank, args=(r, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    got = q.get(timeout=900)
+    got = get_from_ranks(q, procs, timeout=900)
     for p in procs:
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]

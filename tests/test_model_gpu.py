@@ -71,18 +71,57 @@ def test_qwen2_two_layers_benchmark_distribution():
 
 
 def test_cuda_graph_replay_matches_eager_for_new_batches():
-    # One captured forward serves every batch of the same token count: the device
-    # schedule (sequence starts, attention work list) is recomputed inside the graph.
+    # Graphs are keyed on token buckets: a batch is padded with dummy sequences up to its
+    # bucket (1000 -> 1024, 1300 / 1332 -> 1536 tokens); a token count that keeps repeating
+    # (here after 2 occurrences) gets its own unpadded graph.  Either way the device
+    # schedule (sequence starts, attention work list) is recomputed inside the graph, and
+    # every real row equals the eager forward's.
     cfg = synthetic.qwen3_0_6b(num_hidden_layers=2)
     weights = synthetic.awq_weights(cfg, seed=0, device="cuda:0")
     worker = GPUWorker(MESConfig(model_config=cfg), device="cuda:0")
+    worker.exact_after = 2
     load_weights(worker.model, weights)
-    for i, lengths in enumerate([[300, 500, 200], [100, 900], [1000], [1] * 10 + [990]]):
+    batches = [[300, 500, 200], [100, 900], [1000], [1] * 10 + [990], [700, 600], [333] * 4]
+    for i, lengths in enumerate(batches):
         ids, pos, last = synthetic.packed_batch(lengths, cfg.vocab_size, seed=i)
         worker.use_cuda_graphs = True
         got = worker.embed(ids, pos, last).numpy()
         worker.use_cuda_graphs = False
         want = worker.embed(ids, pos, last).numpy()
         assert np.array_equal(got, want), lengths
-    assert len(worker._graphs) == 1 and not worker._no_graph
+    # 1000 tokens: bucket graph (1024) first, then the exact graph from the second batch of
+    # 1000 on; 1300 and 1332 tokens share the 1536-token bucket graph.  (The worker's
+    # default waits for 8 occurrences before an exact graph.)
+    assert worker.captures == 3, worker.captures
+    assert len(worker._graphs) == 2 and len(worker._exact) == 1 and not worker._no_graph
+    # _inference returns the real rows of a padded (bucket) replay: 777 tokens -> 1024.
+    ids, pos, _ = synthetic.packed_batch([400, 377], cfg.vocab_size, seed=9)
+    worker.use_cuda_graphs = True
+    hidden = worker._inference(ids, pos).float().cpu().numpy()
+    worker.use_cuda_graphs = False
+    assert np.array_equal(hidden, worker._inference(ids, pos).float().cpu().numpy())
+    assert worker.captures == 3
+    assert _C.take_device_error() == 0
+
+
+def test_last_rows_only_matches_full_forward():
+    # Last layer's o_proj / MLP / final norm on the pooled rows only: the same embeddings up
+    # to the summation order of those GEMMs (M = B takes the small-batch kernels) and the
+    # final bf16 rounding - cosine >= 0.99999 per row; eager and CUDA-graph paths agree.
+    cfg = synthetic.qwen3_0_6b(num_hidden_layers=3)
+    weights = synthetic.awq_weights(cfg, seed=0, device="cuda:0", norm_noise=0.1)
+    worker = GPUWorker(MESConfig(model_config=cfg), device="cuda:0")
+    load_weights(worker.model, weights)
+    for lengths in ([300, 500, 200], [1] * 7 + [130, 64]):
+        ids, pos, last = synthetic.packed_batch(lengths, cfg.vocab_size, seed=3)
+        full = worker.embed(ids, pos, last).numpy()
+        worker.last_rows_only = True
+        try:
+            graph = worker.embed(ids, pos, last).numpy()
+            worker.use_cuda_graphs = False
+            eager = worker.embed(ids, pos, last).numpy()
+        finally:
+            worker.last_rows_only, worker.use_cuda_graphs = False, True
+        assert np.array_equal(graph, eager), lengths
+        assert _cos(graph, full).min() >= 0.99999, _cos(graph, full)
     assert _C.take_device_error() == 0

@@ -121,9 +121,12 @@ def test_overlap_split_is_a_sequence_start_near_the_middle(monkeypatch):
     assert qwen2.DecoderModel.overlap_split_host(edge) == 2200
     # The model's own path (positions as a torch tensor) applies the same rule.
     import torch
+    import types
     D = qwen2.DecoderModel
-    assert D._overlap_split(D, torch.from_numpy(pos)) == 3000
-    assert D._overlap_split(D, torch.from_numpy(np.concatenate([np.arange(4800), np.arange(200)]))) is None
+    m = types.SimpleNamespace(tp_size=2, overlap_min_tokens=D.overlap_min_tokens,
+                              _nearest_middle=D._nearest_middle)
+    assert D._overlap_split(m, torch.from_numpy(pos)) == 3000
+    assert D._overlap_split(m, torch.from_numpy(np.concatenate([np.arange(4800), np.arange(200)]))) is None
     monkeypatch.setattr(qwen2, "_tp_size", lambda: 1)
     assert qwen2.DecoderModel.overlap_split_host(pos) == NO                    # tp == 1
     assert qwen2.DecoderModel.overlap_reserved_sms(2) == 16
@@ -145,11 +148,13 @@ def test_host_split_is_used_as_given(monkeypatch):
 
     def no_device_read(*args):
         raise AssertionError("device read of the split")
-    monkeypatch.setattr(D, "_overlap_split", no_device_read)
+    import types
+    model = types.SimpleNamespace(tp_size=2, _overlap_split=no_device_read)
     pos_t = torch.from_numpy(one_seq)
-    assert D._resolve_split(D, pos_t, host) is None
-    assert D._resolve_split(D, pos_t, 3000) == 3000
+    assert D._resolve_split(model, pos_t, host) is None
+    assert D._resolve_split(model, pos_t, 3000) == 3000
     with pytest.raises(AssertionError):
-        D._resolve_split(D, pos_t, None)
-    monkeypatch.setattr(qwen2, "_tp_size", lambda: 1)
-    assert D._resolve_split(D, pos_t, None) is None
+        D._resolve_split(model, pos_t, None)
+    model.tp_size = 1                     # e.g. a data-parallel replica in a process group
+    assert D._resolve_split(model, pos_t, None) is None
+    assert D.overlap_split_host(one_seq, tp_size=1) == D.NO_SPLIT

@@ -53,6 +53,7 @@ def _worker(rank, port, q):
     tp_nccl_environment(2)
     dist.init_process_group("nccl", rank=rank, world_size=2, device_id=dev,
                             timeout=datetime.timedelta(seconds=60))
+    worker = None
     try:
         worker, ids, pos, last = _model_and_batch(dev)
         with torch.no_grad():
@@ -60,10 +61,27 @@ def _worker(rank, port, q):
             unsplit = worker.model(ids, pos).float().cpu()
             DecoderModel.overlap_min_tokens = 4096
             overlapped = worker.model(ids, pos).float().cpu()
+        # Bucketed CUDA graphs at tp = 2: each micro-batch is padded to its own bucket (the
+        # 5000-token batch splits at 3000: 3000 -> 3072 and 2000 -> 2048 tokens), so the
+        # graph's micro-batch boundary is fixed by the bucket; real rows equal the eager
+        # forward's.
+        from mes_b200 import synthetic
+        graphs = []
+        for i, lengths in enumerate([LENGTHS, [900, 2100, 1400, 700]]):
+            hids, hpos, hlast = synthetic.packed_batch(lengths, worker.model.model.embed_tokens.weight.shape[0], seed=i)
+            worker.use_cuda_graphs = True
+            got = worker.embed(hids, hpos, hlast).numpy()
+            worker.use_cuda_graphs = False
+            want = worker.embed(hids, hpos, hlast).numpy()
+            graphs.append(bool(np.array_equal(got, want)))
         assert _C.take_device_error() == 0
         if rank == 0:
-            q.put((unsplit.numpy(), overlapped.numpy(), np.asarray(last)))
+            q.put((unsplit.numpy(), overlapped.numpy(), np.asarray(last), graphs,
+                   worker.captures))
     finally:
+        if worker is not None:
+            worker.release_graphs()
+        torch.cuda.synchronize()
         dist.destroy_process_group()
 
 
@@ -76,11 +94,14 @@ def test_tp2_overlapped_forward_matches():
     procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    unsplit, overlapped, last = q.get(timeout=600)
+    from test_configs_gpu import get_from_ranks
+    unsplit, overlapped, last, graphs, captures = get_from_ranks(q, procs, timeout=600)
     for p in procs:
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert np.array_equal(unsplit, overlapped)
+    assert all(graphs), graphs
+    assert captures == 2, captures     # bucket layouts (3072, 2048) and (3072, 2304)
 
     worker, ids, pos, _ = _model_and_batch(torch.device("cuda", 0))
     with torch.no_grad():
