@@ -247,6 +247,26 @@ int mes_awq_gemm_ws(int epilogue, const void* X, int64_t ldx, const int32_t* qwe
                     int64_t ldy, int64_t M, int64_t N, int64_t K, int group_size,
                     void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Weight panels for mes_awq_gemm_on_panel: panel i = bf16 W^T [N[i], K[i]] (row n = output
+ * feature n, K contiguous, 16-byte aligned) of the kernel-layout AWQ tensors qweight_mes[i],
+ * qzeros[i], scales[i], with the GEMM's exact dequantisation.  1 <= count <= 8; the pointer
+ * and size arrays are host memory, the tensors device memory.  One launch builds all of
+ * them - e.g. the four projections of a decoder layer, shared by both tensor-parallel
+ * micro-batches.  Part of the same replacement of the dense F.linear of
+ * layers/linear.py:54,86,179 as mes_awq_gemm. */
+int mes_awq_panels(int count, const int32_t* const* qweight_mes, const int32_t* const* qzeros,
+                   const void* const* scales, const int64_t* K, const int64_t* N,
+                   void* const* panels, void* stream);
+
+/* The GEMM of mes_awq_gemm_ws (same `epilogue` codes, Y and bias conventions) with its
+ * weights given as a prepared panel (mes_awq_panels) instead of AWQ tensors.  Only for
+ * shapes that take the panel path: mes_awq_gemm_workspace_size(M, N, K) > 0 (M > 256,
+ * N % 256 == 0); otherwise MES_ERR_INVALID.  Replaces the same projections
+ * (layers/linear.py:90-180). */
+int mes_awq_gemm_on_panel(int epilogue, const void* X, int64_t ldx, const void* panel,
+                          const void* bias, void* Y, int64_t ldy, int64_t M, int64_t N,
+                          int64_t K, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

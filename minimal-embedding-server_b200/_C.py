@@ -49,6 +49,8 @@ SIGNATURES = {
                                      _i32, _vp]),
     "mes_awq_gemm_silu": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp]),
     "mes_awq_gemm_workspace_size": (_i64, [_i64, _i64, _i64]),
+    "mes_awq_panels": (_i32, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "mes_awq_gemm_on_panel": (_i32, [_i32, _vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "mes_awq_gemm_ws": (_i32, [_i32, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                _i32, _vp, _i64, _vp]),
 }
@@ -311,20 +313,52 @@ _EPI_NAME = {EPI_BF16: "bf16", EPI_RESIDUAL: "residual", EPI_SILU: "silu"}
 use_gemm_workspace = True
 
 
+def gemm_uses_panel(M: int, N: int, K: int) -> bool:
+    """Whether a GEMM of this shape runs on a dequantised weight panel (M > 256 tokens,
+    N % 256 == 0), when the wrappers use workspaces at all."""
+    return use_gemm_workspace and int(lib().mes_awq_gemm_workspace_size(M, N, K)) > 0
+
+
+def awq_panels(weights, panels) -> None:
+    """Build the bf16 weight panels ``panels[i]`` (``[N, K]``, from ``torch.empty``) of the
+    kernel-layout AWQ tensors ``weights[i] = (qweight_mes, qzeros, scales)`` in one launch
+    (``mes_awq_panels``; at most 8)."""
+    n = len(weights)
+    _need(0 < n <= 8 and len(panels) == n, "1..8 panels")
+    arr = lambda vals, t: (t * n)(*vals)
+    qw = arr([_p(w[0]) for w in weights], _vp)
+    qz = arr([_p(w[1]) for w in weights], _vp)
+    sc = arr([_p(w[2]) for w in weights], _vp)
+    K = arr([w[0].shape[0] * 8 for w in weights], _i64)
+    N = arr([w[0].shape[1] for w in weights], _i64)
+    for (w, p_) in zip(weights, panels):
+        _need(p_.dtype == torch.bfloat16 and p_.is_contiguous()
+              and tuple(p_.shape) == (w[0].shape[1], w[0].shape[0] * 8), "panel must be bf16 [N, K]")
+    _check(lib().mes_awq_panels(n, qw, qz, sc, K, N, arr([_p(p_) for p_ in panels], _vp),
+                                _stream(panels[0])), "mes_awq_panels")
+
+
 def _awq_gemm_call(epi: int, x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
-                   scales: torch.Tensor, bias, y: torch.Tensor, group_size: int) -> None:
+                   scales: torch.Tensor, bias, y: torch.Tensor, group_size: int,
+                   panel: torch.Tensor | None = None) -> None:
     K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
     M = x.shape[0]
-    ws_bytes = int(lib().mes_awq_gemm_workspace_size(M, N, K)) if use_gemm_workspace else 0
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes > 0 else None
     ev = gemm_events if gemm_event_kinds is None or _EPI_NAME[epi] in gemm_event_kinds else None
     if ev is not None:
         e0, e1 = _timing_event(), _timing_event()
         e0.record()
-    _check(lib().mes_awq_gemm_ws(epi, _p(x), x.stride(0), _p(qweight_mes), _p(qzeros),
-                                 _p(scales), _p(bias), _p(y), y.stride(0), M, N, K, group_size,
-                                 _p(ws), ws_bytes, _stream(x)),
-           f"mes_awq_gemm ({_EPI_NAME[epi]} epilogue)", 2 if ws is not None else 1)
+    if panel is not None and gemm_uses_panel(M, N, K):
+        _need(tuple(panel.shape) == (N, K) and panel.dtype == torch.bfloat16, "panel must be bf16 [N, K]")
+        _check(lib().mes_awq_gemm_on_panel(epi, _p(x), x.stride(0), _p(panel), _p(bias), _p(y),
+                                           y.stride(0), M, N, K, _stream(x)),
+               f"mes_awq_gemm_on_panel ({_EPI_NAME[epi]} epilogue)")
+    else:
+        ws_bytes = int(lib().mes_awq_gemm_workspace_size(M, N, K)) if use_gemm_workspace else 0
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes > 0 else None
+        _check(lib().mes_awq_gemm_ws(epi, _p(x), x.stride(0), _p(qweight_mes), _p(qzeros),
+                                     _p(scales), _p(bias), _p(y), y.stride(0), M, N, K, group_size,
+                                     _p(ws), ws_bytes, _stream(x)),
+               f"mes_awq_gemm ({_EPI_NAME[epi]} epilogue)", 2 if ws is not None else 1)
     if ev is not None:
         e1.record()
         ev.append((e0, e1, 2.0 * M * N * K, (_EPI_NAME[epi], M, N, K)))
@@ -332,7 +366,8 @@ def _awq_gemm_call(epi: int, x: torch.Tensor, qweight_mes: torch.Tensor, qzeros:
 
 def awq_gemm_residual(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
                       scales: torch.Tensor, residual: torch.Tensor,
-                      bias: torch.Tensor | None = None, group_size: int = 128) -> torch.Tensor:
+                      bias: torch.Tensor | None = None, group_size: int = 128,
+                      panel: torch.Tensor | None = None) -> torch.Tensor:
     """``residual[M, N] (fp32) += x @ W (+ bias)`` in the GEMM epilogue."""
     _need(x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(-1) == 1,
           "x must be bf16 [M, K] with unit inner stride")
@@ -340,13 +375,13 @@ def awq_gemm_residual(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.
     K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
     M = x.shape[0]
     _need(x.shape[1] == K and tuple(residual.shape) == (M, N), "shape mismatch")
-    _awq_gemm_call(EPI_RESIDUAL, x, qweight_mes, qzeros, scales, bias, residual, group_size)
+    _awq_gemm_call(EPI_RESIDUAL, x, qweight_mes, qzeros, scales, bias, residual, group_size, panel)
     return residual
 
 
 def awq_gemm_silu(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
                   scales: torch.Tensor, out: torch.Tensor | None = None,
-                  group_size: int = 128) -> torch.Tensor:
+                  group_size: int = 128, panel: torch.Tensor | None = None) -> torch.Tensor:
     """``silu(x @ Wg) * (x @ Wu)`` with the gate/up columns interleaved in blocks of 16
     (see ``interleave_gate_up``); output ``[M, N/2]`` bf16."""
     _need(x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(-1) == 1,
@@ -356,7 +391,7 @@ def awq_gemm_silu(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tens
     _need(x.shape[1] == K, f"x has K={x.shape[1]}, weight has K={K}")
     if out is None:
         out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=x.device)
-    _awq_gemm_call(EPI_SILU, x, qweight_mes, qzeros, scales, None, out, group_size)
+    _awq_gemm_call(EPI_SILU, x, qweight_mes, qzeros, scales, None, out, group_size, panel)
     return out
 
 
@@ -376,7 +411,8 @@ def interleave_gate_up(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torc
 
 def awq_gemm(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
              scales: torch.Tensor, bias: torch.Tensor | None = None,
-             out: torch.Tensor | None = None, group_size: int = 128) -> torch.Tensor:
+             out: torch.Tensor | None = None, group_size: int = 128,
+             panel: torch.Tensor | None = None) -> torch.Tensor:
     """``x[M, K] @ W[K, N] (+ bias)`` with W given by AWQ tensors in the kernel layout."""
     _need(x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(-1) == 1,
           "x must be bf16 [M, K] with unit inner stride")
@@ -385,5 +421,5 @@ def awq_gemm(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
     _need(x.shape[1] == K, f"x has K={x.shape[1]}, weight has K={K}")
     if out is None:
         out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
-    _awq_gemm_call(EPI_BF16, x, qweight_mes, qzeros, scales, bias, out, group_size)
+    _awq_gemm_call(EPI_BF16, x, qweight_mes, qzeros, scales, bias, out, group_size, panel)
     return out

@@ -422,7 +422,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
 varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
                              __nv_bfloat16* __restrict__ out, const int* __restrict__ hdr,
                              const int* __restrict__ cu, const int2* __restrict__ items, int Hq,
-                             int Hkv, float scale_log2) {
+                             int Hkv, float scale_log2, int l2_hints) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -482,6 +482,14 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
    if (warp == 8) {
     // ------------------------------------ TMA ----------------------------------------
     if (lane == 0) {
+      // Each K/V tile is read by every query tile of its sequence, spread over time; each Q
+      // tile once.  Keep K/V in L2 in preference to Q.
+      const uint64_t pol_kv = mes::l2_policy_evict_last();
+      const uint64_t pol_q = mes::l2_policy_evict_first();
+      auto load = [&](void* dst, uint64_t* bar, int x, int y, uint64_t pol) {
+        if (l2_hints) mes::tma_load_2d_hint(dst, &map_qkv, bar, x, y, pol);
+        else mes::tma_load_2d(dst, &map_qkv, bar, x, y);
+      };
       int n_item = 0, kt = 0, vt = 0, q_issued = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < num_work && ok; w = snake(++n_item, blockIdx.x, gridDim.x)) {
@@ -497,7 +505,7 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
         mes::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
 #pragma unroll
         for (int c = 0; c < 4; ++c)
-          mes::tma_load_2d(qs + c * (kQBytes / 2), &map_qkv, q_full, h0 * kD + c * 64, q0);
+          load(qs + c * (kQBytes / 2), q_full, h0 * kD + c * 64, q0, pol_q);
         const int kcol = (Hq + g) * kD, vcol = (Hq + Hkv + g) * kD;
         for (int j = 0; j <= it.y; ++j) {
           const int k0 = start + j * kTile;
@@ -509,8 +517,8 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
           }
           uint8_t* kd = ks + ks_ * kKVBytes;
           mes::mbar_arrive_expect_tx(&k_full[ks_], kKVBytes);
-          mes::tma_load_2d(kd, &map_qkv, &k_full[ks_], kcol, k0);
-          mes::tma_load_2d(kd + kKVBytes / 2, &map_qkv, &k_full[ks_], kcol + 64, k0);
+          load(kd, &k_full[ks_], kcol, k0, pol_kv);
+          load(kd + kKVBytes / 2, &k_full[ks_], kcol + 64, k0, pol_kv);
           ++kt;
           if (vt >= kKVStages &&
               !mes::mbar_wait(&v_empty[vs_], ((vt / kKVStages) & 1) ^ 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) {
@@ -519,8 +527,8 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
           }
           uint8_t* vd = vs + vs_ * kKVBytes;
           mes::mbar_arrive_expect_tx(&v_full[vs_], kKVBytes);
-          mes::tma_load_2d(vd, &map_qkv, &v_full[vs_], vcol, k0);
-          mes::tma_load_2d(vd + kKVBytes / 2, &map_qkv, &v_full[vs_], vcol + 64, k0);
+          load(vd, &v_full[vs_], vcol, k0, pol_kv);
+          load(vd + kKVBytes / 2, &v_full[vs_], vcol + 64, k0, pol_kv);
           ++vt;
         }
       }
@@ -786,6 +794,16 @@ static int poly_pairs() {
   return v;
 }
 
+// L2 cache hints on the head-pair kernel's loads (K/V evict_last, Q evict_first);
+// MES_ATTN_L2_HINTS=0 turns them off for measurements.
+static int l2_hints() {
+  static const int v = [] {
+    const char* e = getenv("MES_ATTN_L2_HINTS");
+    return (e && atoi(e) == 0) ? 0 : 1;
+  }();
+  return v;
+}
+
 // The head-pair kernel's register split must fit in what each SM sub-partition holds for
 // the CTA at launch: three warps per sub-partition, one of them shrinking.
 template <typename K>
@@ -835,7 +853,7 @@ extern "C" int mes_varlen_attention(const void* qkv, int64_t ld, void* out, cons
     if (st != MES_OK) return st;
     kern<<<grid, kPThreads, kPSmem, s>>>(map, (__nv_bfloat16*)out, (const int*)ws,
                                          (const int*)(ws + 256), (const int2*)(ws + items_off),
-                                         Hq, Hkv, scale_log2);
+                                         Hq, Hkv, scale_log2, l2_hints());
     return mes_host::from_cuda(cudaGetLastError());
   }
   static std::atomic<uint64_t> attr_done1{0};

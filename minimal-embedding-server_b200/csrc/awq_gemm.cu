@@ -1186,28 +1186,47 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
 
 // ------------------------------------ weight panel ----------------------------------------
 // W^T [N, K] bf16 (K contiguous) from the kernel-layout AWQ tensors, with the GEMM's exact
-// dequantisation: the A operand of the PANEL pair kernel.  A block of 256 threads covers 8
-// features x 32 words (256 k): warp f takes feature n0 + f, lane b word b0 + b, so a warp
-// writes 512 contiguous bytes of its feature's row, and the eight warps read the same 32
-// sectors of the packed words (one per word row, eight features each) through L1.
-__global__ void __launch_bounds__(256) awq_panel_kernel(const uint32_t* __restrict__ qw,
-                                                        const int32_t* __restrict__ qzeros,
-                                                        const uint16_t* __restrict__ scales,
-                                                        int K, int N, uint4* __restrict__ out) {
+// dequantisation: the A operand of the PANEL pair kernel.  One launch builds up to
+// kMaxPanels panels (the projections of one decoder layer).  A block of 256 threads covers
+// 8 features x 32 words (256 k) of one panel: warp f takes feature n0 + f, lane b word
+// b0 + b, so a warp writes 512 contiguous bytes of its feature's row, and the eight warps
+// read the same 32 sectors of the packed words (one per word row, eight features each)
+// through L1.
+constexpr int kMaxPanels = 8;
+struct PanelJob {
+  const uint32_t* qw;
+  const int32_t* qzeros;
+  const uint16_t* scales;
+  uint4* out;
+  int K, N;
+  int kblocks;      // blocks along K: ceil(K / 8 / 32)
+  int first_block;  // first block index of this panel in the launch
+};
+struct PanelJobs {
+  PanelJob job[kMaxPanels];
+  int count;
+};
+
+__global__ void __launch_bounds__(256) awq_panel_kernel(const __grid_constant__ PanelJobs jobs) {
+  int p = 0;
+  while (p + 1 < jobs.count && (int)blockIdx.x >= jobs.job[p + 1].first_block) ++p;
+  const PanelJob& jb = jobs.job[p];
+  const int local = blockIdx.x - jb.first_block;
   const int f = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.y * 8 + f;
-  const int b = blockIdx.x * 32 + lane;
-  if (b >= K / 8) return;
+  const int n = (local / jb.kblocks) * 8 + f;
+  const int b = (local % jb.kblocks) * 32 + lane;
+  if (b >= jb.K / 8) return;
+  const int N = jb.N;
   const int g = (8 * b) / kGroup;
-  const GroupParams gp = make_group(__ldg(qzeros + (int64_t)g * (N / 8) + (n >> 3)),
-                                    4 * kInvOrder[n & 7], __ldg(scales + (int64_t)g * N + n));
-  const uint32_t w = __ldg(qw + (int64_t)b * N + n);
+  const GroupParams gp = make_group(__ldg(jb.qzeros + (int64_t)g * (N / 8) + (n >> 3)),
+                                    4 * kInvOrder[n & 7], __ldg(jb.scales + (int64_t)g * N + n));
+  const uint32_t w = __ldg(jb.qw + (int64_t)b * N + n);
   uint4 v;
   v.x = dq_pair(w, gp);
   v.y = dq_pair(w >> 4, gp);
   v.z = dq_pair(w >> 8, gp);
   v.w = dq_pair(w >> 12, gp);
-  out[(int64_t)n * (K / 8) + b] = v;
+  jb.out[(int64_t)n * (jb.K / 8) + b] = v;
 }
 
 // ------------------------------------ repack ----------------------------------------------
@@ -1473,13 +1492,39 @@ int launch_gemm_pair(const void* X, int64_t ldx, const void* w, const int32_t* q
   return mes_host::from_cuda(cudaGetLastError());
 }
 
-// The weight panel W^T [N, K] bf16 of one GEMM (see awq_panel_kernel).
+// Weight panels W^T [N_i, K_i] bf16 of up to kMaxPanels GEMMs in one launch (see
+// awq_panel_kernel).
+int launch_panels(int count, const int32_t* const* qw, const int32_t* const* qzeros,
+                  const void* const* scales, const int64_t* K, const int64_t* N,
+                  void* const* panels, cudaStream_t stream) {
+  if (count < 1 || count > kMaxPanels) return MES_ERR_INVALID;
+  PanelJobs jobs = {};
+  int64_t blocks = 0;
+  for (int i = 0; i < count; ++i) {
+    if (!qw[i] || !qzeros[i] || !scales[i] || !panels[i]) return MES_ERR_INVALID;
+    if (K[i] <= 0 || N[i] <= 0 || K[i] % kGroup || N[i] % 8 || K[i] > (1 << 24) || N[i] > (1 << 24))
+      return MES_ERR_INVALID;
+    if (reinterpret_cast<uintptr_t>(panels[i]) & 15) return MES_ERR_ALIGN;
+    PanelJob& j = jobs.job[i];
+    j.qw = (const uint32_t*)qw[i];
+    j.qzeros = qzeros[i];
+    j.scales = (const uint16_t*)scales[i];
+    j.out = (uint4*)panels[i];
+    j.K = (int)K[i];
+    j.N = (int)N[i];
+    j.kblocks = (int)((K[i] / 8 + 31) / 32);
+    j.first_block = (int)blocks;
+    blocks += (int64_t)j.kblocks * (N[i] / 8);
+  }
+  if (blocks > (1ll << 31) - 1) return MES_ERR_INVALID;
+  jobs.count = count;
+  awq_panel_kernel<<<(unsigned)blocks, 256, 0, stream>>>(jobs);
+  return mes_host::from_cuda(cudaGetLastError());
+}
+
 int launch_panel(const int32_t* qw, const int32_t* qzeros, const void* scales, int64_t N,
                  int64_t K, void* panel, cudaStream_t stream) {
-  const dim3 grid((unsigned)((K / 8 + 31) / 32), (unsigned)(N / 8), 1);
-  awq_panel_kernel<<<grid, 256, 0, stream>>>((const uint32_t*)qw, qzeros, (const uint16_t*)scales,
-                                            (int)K, (int)N, (uint4*)panel);
-  return mes_host::from_cuda(cudaGetLastError());
+  return launch_panels(1, &qw, &qzeros, &scales, &K, &N, &panel, stream);
 }
 
 // Whether the GEMM of this shape takes the panel path when given a workspace: batches of
@@ -1491,7 +1536,7 @@ bool panel_path(int64_t M, int64_t N, int64_t K) {
     const char* v = getenv("MES_GEMM_PANEL");
     return !(v && atoi(v) == 0);
   }();
-  return enabled && M > 256 && N % (2 * kBN) == 0 && N / 8 <= 65535 && K <= (1 << 24);
+  return enabled && M > 256 && N % (2 * kBN) == 0 && N <= (1 << 24) && K <= (1 << 24);
 }
 
 // Tile configuration for M > 64 tokens.  The environment variable MES_GEMM_CONFIG (read
@@ -1655,4 +1700,35 @@ extern "C" int mes_awq_gemm_silu(const void* X, int64_t ldx, const int32_t* qwei
                                  int64_t M, int64_t N, int64_t K, int group_size, void* stream) {
   return mes_awq_gemm_ws(kEpiSilu, X, ldx, qweight_mes, qzeros, scales, nullptr, Y, ldy, M, N, K,
                          group_size, nullptr, 0, stream);
+}
+
+extern "C" int mes_awq_panels(int count, const int32_t* const* qweight_mes,
+                              const int32_t* const* qzeros, const void* const* scales,
+                              const int64_t* K, const int64_t* N, void* const* panels,
+                              void* stream) {
+  if (!qweight_mes || !qzeros || !scales || !K || !N || !panels) return MES_ERR_INVALID;
+  return launch_panels(count, qweight_mes, qzeros, scales, K, N, panels, (cudaStream_t)stream);
+}
+
+extern "C" int mes_awq_gemm_on_panel(int epilogue, const void* X, int64_t ldx, const void* panel,
+                                     const void* bias, void* Y, int64_t ldy, int64_t M, int64_t N,
+                                     int64_t K, void* stream) {
+  if (epilogue < kEpiBf16 || epilogue > kEpiSilu) return MES_ERR_INVALID;
+  if (epilogue == kEpiSilu && bias) return MES_ERR_INVALID;
+  if (M < 0 || N <= 0 || K <= 0 || K % kGroup || ldx < K || ldx % 8) return MES_ERR_INVALID;
+  const int64_t y_cols = epilogue == kEpiSilu ? N / 2 : N;
+  if (ldy < y_cols || (epilogue != kEpiResidual && ldy % 8)) return MES_ERR_INVALID;
+  if (M == 0) return MES_OK;
+  if (!panel_path(M, N, K) || !X || !panel || !Y) return MES_ERR_INVALID;
+  const bool y_ok = epilogue == kEpiResidual ? (reinterpret_cast<uintptr_t>(Y) & 3) == 0 : aligned16(Y);
+  if (!aligned16(X) || !aligned16(panel) || !y_ok) return MES_ERR_ALIGN;
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (epilogue) {
+    case kEpiBf16:
+      return launch_gemm_pair<kEpiBf16, true>(X, ldx, panel, nullptr, nullptr, bias, Y, ldy, M, N, K, s);
+    case kEpiResidual:
+      return launch_gemm_pair<kEpiResidual, true>(X, ldx, panel, nullptr, nullptr, bias, Y, ldy, M, N, K, s);
+    default:
+      return launch_gemm_pair<kEpiSilu, true>(X, ldx, panel, nullptr, nullptr, nullptr, Y, ldy, M, N, K, s);
+  }
 }

@@ -65,6 +65,9 @@ class LinearBase(nn.Module):
         self.quant_config = quant_config or AWQConfig()
         self.group_size = self.quant_config.group_size
         self._qweight_mes = None  # kernel layout, built by process_weights_after_loading()
+        # bf16 weight panel W^T [n_local, k_local] prepared by the owning decoder layer for
+        # the current forward (see DecoderLayer.build_panels); None: the GEMM builds its own.
+        self.panel = None
 
     def _create_weights(self, k_local: int, n_local: int, bias: bool, bias_size: int):
         G = self.group_size
@@ -116,12 +119,20 @@ class LinearBase(nn.Module):
         """Repack ``qweight`` into the kernel layout on the parameter's device (once)."""
         self._qweight_mes = _C.awq_repack(self.qweight.data.contiguous())
 
-    def _mm(self, x: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+    def gemm_weights(self):
+        """``(qweight_mes, qzeros, scales)`` of the kernel layout this layer's GEMM uses."""
         if self._qweight_mes is None or self._qweight_mes.device != self.qweight.device:
             self.process_weights_after_loading()
+        return self._qweight_mes, self.qzeros, self.scales
+
+    def _mm(self, x: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+        """Plain GEMM in the checkpoint's column order (the prepared panel is used only when
+        it was built from these weights, not from a fused-epilogue layout)."""
+        qw, qz, sc = LinearBase.gemm_weights(self)
+        panel = self.panel if self.gemm_weights()[0] is qw else None
         shape = x.shape
-        y = _C.awq_gemm(x.reshape(-1, shape[-1]), self._qweight_mes, self.qzeros,
-                        self.scales, bias, group_size=self.group_size)
+        y = _C.awq_gemm(x.reshape(-1, shape[-1]), qw, qz, sc, bias, group_size=self.group_size,
+                        panel=panel)
         return y.view(*shape[:-1], y.shape[-1])
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -207,14 +218,23 @@ class MergedColumnParallelLinear(ColumnParallelLinear):
                 and (self.output_size_per_partition // 2) % 64 == 0
                 and self.output_size_per_partition % 128 == 0 and self.bias is None)
 
-    def forward_silu(self, x: torch.Tensor) -> torch.Tensor:
-        """``SiluAndMul(self(x))`` as one GEMM: the epilogue multiplies silu(gate) by up
-        (``layers/activation.py:12-14``), so the [T, 2I] projection never reaches HBM."""
+    def gemm_weights(self):
+        """The gate/up-interleaved pack when the fused SiLU GEMM applies, else the plain
+        kernel layout."""
+        if not self.supports_silu():
+            return super().gemm_weights()
         pack = getattr(self, "_silu_pack", None)
         if pack is None or pack[0].device != self.qweight.device:
             pack = self._silu_pack = self._build_silu_pack()
+        return pack
+
+    def forward_silu(self, x: torch.Tensor) -> torch.Tensor:
+        """``SiluAndMul(self(x))`` as one GEMM: the epilogue multiplies silu(gate) by up
+        (``layers/activation.py:12-14``), so the [T, 2I] projection never reaches HBM."""
+        pack = self.gemm_weights()
         shape = x.shape
-        y = _C.awq_gemm_silu(x.reshape(-1, shape[-1]), *pack, group_size=self.group_size)
+        y = _C.awq_gemm_silu(x.reshape(-1, shape[-1]), *pack, group_size=self.group_size,
+                             panel=self.panel)
         return y.view(*shape[:-1], y.shape[-1])
 
 
@@ -284,9 +304,8 @@ class RowParallelLinear(LinearBase):
         with an all-reduce and returned for the following add+RMSNorm to apply."""
         if self.tp_size > 1:
             return self.forward(x)
-        if self._qweight_mes is None or self._qweight_mes.device != self.qweight.device:
-            self.process_weights_after_loading()
-        _C.awq_gemm_residual(x.reshape(-1, x.shape[-1]), self._qweight_mes, self.qzeros,
-                             self.scales, residual.view(-1, residual.shape[-1]), self.bias,
-                             group_size=self.group_size)
+        qw, qz, sc = self.gemm_weights()
+        _C.awq_gemm_residual(x.reshape(-1, x.shape[-1]), qw, qz, sc,
+                             residual.view(-1, residual.shape[-1]), self.bias,
+                             group_size=self.group_size, panel=self.panel)
         return None

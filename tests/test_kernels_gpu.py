@@ -451,7 +451,22 @@ def test_awq_gemm_panel_equals_fused(M, K, N):
             outs[panel] = (r, y, z)
         finally:
             _C.use_gemm_workspace = True
+    # Panels prepared in one batched launch (as a decoder layer does) and passed in give the
+    # same result as the per-call workspace.
+    qwi, qzi, sci = _C.interleave_gate_up(qw, qz, sc)
+    qwim = _C.awq_repack(qwi)
+    pa = torch.empty(N, K, dtype=torch.bfloat16, device=DEV)
+    pb = torch.empty(N, K, dtype=torch.bfloat16, device=DEV)
+    _C.awq_panels([(qwm, qz, sc), (qwim, qzi, sci)], [pa, pb])
+    w_ref = _C.awq_dequant(qwm, qz, sc)                  # W^T [N, K], the GEMM's arithmetic
+    assert torch.equal(pa, w_ref)
+    r = r0.clone()
+    _C.awq_gemm_residual(x, qwm, qz, sc, r, panel=pa)
+    y = _C.awq_gemm(x, qwm, qz, sc, panel=pa)
+    z = _C.awq_gemm_silu(x, qwim, qzi, sci, panel=pb)
     assert _C.take_device_error() == 0
+    assert torch.equal(r, outs[True][0]) and torch.equal(y, outs[True][1])
+    assert torch.equal(z, outs[True][2])
     assert torch.equal(outs[True][0], outs[False][0])
     for a, b in zip(outs[True][1:], outs[False][1:]):
         a, b = a.float(), b.float()

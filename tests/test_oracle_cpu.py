@@ -166,6 +166,9 @@ def test_host_argument_checks_reject_without_gpu_work():
     assert lib.mes_awq_gemm_workspace_size(20000, 384, 1024) == 0
     assert lib.mes_awq_gemm_ws(3, None, 64, None, None, None, None, None, 64, 16, 128, 64, 128,
                                None, 0, None) == 1
+    assert lib.mes_awq_gemm_on_panel(0, None, 1024, None, None, None, 1024, 256, 1024, 1024,
+                                     None) == 1     # M <= 256: no panel path
+    assert lib.mes_awq_panels(0, None, None, None, None, None, None, None) == 1
     assert lib.mes_wait_probe(0, 0, None) == 1             # limit out of range
     assert lib.mes_wait_probe(1_000_000_000, 0, None) == 1
 
