@@ -37,12 +37,11 @@ sys.path.insert(0, ROOT)
 
 METRIC = "embedding tokens/sec (20x1000-tok batch)"
 
-# DRAM bytes (read + write) of one launch of the kernel, from `ncu --set full` captures of
-# the same command on one B200 (layer 0 of the 20 x 1000-token forward); None where not
-# captured.
+# DRAM bytes (read + write) of one launch of the kernel, from an `ncu --set full` capture of
+# the same launch shape on one B200 (`--workload c3`, cold L2); None where not captured.
 MEASURED_TRAFFIC: dict = {
-    ("silu", 20000, 6144, 1024): 117.3e6,       # gate_up + SiLU-and-mul, layer 0
-    ("residual", 20000, 1024, 2048): 205.7e6,   # o_proj (CTA pairs), layer 0
+    # gate_up + SiLU-and-mul on the weight panel (CTA-pair kernel), M = 20000
+    ("silu", 20000, 6144, 1024): 133.0e6,
 }
 UNIT = "tokens/s"
 
