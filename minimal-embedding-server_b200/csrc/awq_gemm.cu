@@ -1472,8 +1472,12 @@ int launch_gemm_pair(const void* X, int64_t ldx, const void* w, const int32_t* q
   const int64_t tiles = num_n * ((M + C::kTileT - 1) / C::kTileT);
   const int64_t max_pairs = clusters < mes_host::persistent_ctas() / 2 ? clusters : mes_host::persistent_ctas() / 2;
   // A last round of at most half the pairs runs as half tiles on twice as many pairs.
+  static const bool half_tail = [] {
+    const char* v = getenv("MES_GEMM_HALF_TAIL");
+    return !(v && atoi(v) == 0);
+  }();
   const int64_t left = tiles % max_pairs;
-  const int64_t full = (left != 0 && 2 * left <= max_pairs) ? tiles - left : tiles;
+  const int64_t full = (half_tail && left != 0 && 2 * left <= max_pairs) ? tiles - left : tiles;
   const int64_t items = full + 2 * (tiles - full);
   const int64_t pairs = items < max_pairs ? items : max_pairs;
   // Band of feature tiles walked at a time: the panel rows of a band (about 40 MB at most)

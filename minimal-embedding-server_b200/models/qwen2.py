@@ -250,9 +250,6 @@ class DecoderModel(nn.Module):
         # group created later - e.g. for data-parallel replicas - does not shard the model).
         self.tp_size = _tp_size()
 
-    # Tensor parallelism with the rows of the residual stream sharded over the ranks (see
-    # _forward_seq_parallel); MES_TP_SEQ_PARALLEL=0 keeps the all-reduce form everywhere.
-    seq_parallel = os.environ.get("MES_TP_SEQ_PARALLEL", "1") != "0"
     # Tensor parallelism: below this many tokens the batch is not split for overlap.
     overlap_min_tokens = int(os.environ.get("MES_TP_OVERLAP_MIN_TOKENS", "4096"))
     # Neither micro-batch may have 256 tokens or fewer: the GEMMs split K over clusters for
@@ -292,11 +289,6 @@ class DecoderModel(nn.Module):
         caller knows it from the host copy of the batch (see :meth:`overlap_split_host`,
         ``NO_SPLIT`` when there is none); ``None`` derives it from ``positions``."""
         split = self._resolve_split(positions, overlap_split)
-        T = positions.shape[0]
-        if self.tp_size > 1 and self.seq_parallel:
-            parts = ((0, T),) if split is None else ((0, split), (split, T))
-            if all((b - a) % self.tp_size == 0 for a, b in parts):
-                return self._forward_seq_parallel(input_ids, positions, parts)
         if split is not None:
             return self._forward_overlapped(input_ids, positions, split)
         with batch_schedule(positions):
@@ -353,100 +345,6 @@ class DecoderModel(nn.Module):
         if len(starts) == 0:
             return None
         return int(starts[np.argmin(np.abs(starts - T // 2))])
-
-    def _forward_seq_parallel(self, input_ids, positions, parts) -> torch.Tensor:
-        """Tensor-parallel forward with the residual stream sharded by rows (sequence
-        parallelism).  The reference all-reduces every row-parallel partial product
-        (``layers/linear.py:176-180``) and then adds and normalises all T rows on every
-        rank.  Here the same sum is formed by a reduce-scatter, so each rank adds and
-        normalises only its T / tp rows of the fp32 residual, and an all-gather hands every
-        rank the whole normalised bf16 input of the next column-parallel projection: the
-        bytes on NVLink are those of the all-reduce (all-reduce = reduce-scatter +
-        all-gather), while the norms and residual updates shrink tp-fold.
-
-        ``parts``: one or two micro-batches of whole sequences, each a multiple of tp rows.
-        With two, the compute stream runs them interleaved per half-block (A's attention,
-        B's attention, A's MLP, ...) and each half-block's reduce-scatter -> add + RMSNorm
-        -> all-gather chain runs on a side stream while the other micro-batch computes; the
-        next half-block waits for its all-gather.  Each row's arithmetic is the same as in
-        the all-reduce form (a two-rank sum does not depend on the collective's order)."""
-        n, r = self.tp_size, dist.get_rank()
-        T = positions.shape[0]
-        H = self.embed_tokens.embedding_dim
-        dev = positions.device
-        pos = [positions[a:b] for a, b in parts]
-        loc = [(a + r * (b - a) // n, a + (r + 1) * (b - a) // n) for a, b in parts]
-        comm = self._side_stream(dev)
-        main = torch.cuda.current_stream(dev)
-        comm.wait_stream(main)
-        overlap = len(parts) > 1
-        if overlap:
-            _C.set_sm_reserve(self.overlap_reserved_sms(n))
-        try:
-            schedules = [batch_schedule(p) for p in pos]
-            for ctx in schedules:
-                ctx.__enter__()
-            try:
-                res = [self.embed_tokens.forward_f32(input_ids[lo:hi]) for lo, hi in loc]
-                x_full = [torch.empty(b - a, H, dtype=torch.bfloat16, device=dev) for a, b in parts]
-                gathered = [None] * len(parts)
-
-                def norm_gather(norm, m, delta=None, work=None, out=None):
-                    """(wait for the reduce-scatter) add + RMSNorm of rank-local rows, then
-                    all-gather them into x_full[m] (or `out`); on the side stream when the
-                    micro-batches overlap."""
-                    stream = comm if overlap else main
-                    with torch.cuda.stream(stream):
-                        if work is not None:
-                            work.wait()
-                            if overlap:   # allocated on the compute stream, read here
-                                delta.record_stream(comm)
-                        x_loc = norm.residual_norm(res[m], delta)
-                        dst = x_full[m] if out is None else out
-                        gathered[m] = dist.all_gather_into_tensor(dst, x_loc, async_op=True)
-
-                def take(m):
-                    gathered[m].wait()          # on the compute stream
-                    return x_full[m]
-
-                def scatter(y, m):
-                    d = torch.empty(y.shape[0] // n, H, dtype=torch.bfloat16, device=dev)
-                    return d, dist.reduce_scatter_tensor(d, y, async_op=True)
-
-                for m in range(len(parts)):
-                    norm_gather(self.layers[0].input_layernorm, m)
-                for i, layer in enumerate(self.layers):
-                    nxt = self.layers[i + 1].input_layernorm if i + 1 < len(self.layers) else None
-                    layer.build_panels(min(b - a for a, b in parts))
-                    pend = []
-                    for m in range(len(parts)):
-                        pend.append(scatter(layer.self_attn.forward_partial(pos[m], take(m)), m))
-                        norm_gather(layer.post_attention_layernorm, m, *pend[m])
-                    pend = []
-                    for m in range(len(parts)):
-                        pend.append(scatter(layer.mlp.forward_partial(take(m)), m))
-                        if nxt is not None:
-                            norm_gather(nxt, m, *pend[m])
-                    layer.clear_panels()
-                out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
-                for m, (a, b) in enumerate(parts):
-                    norm_gather(self.norm, m, *pend[m], out=out[a:b])
-                for m in range(len(parts)):
-                    gathered[m].wait()
-                main.wait_stream(comm)
-                return out
-            finally:
-                for ctx in reversed(schedules):
-                    ctx.__exit__(None, None, None)
-        finally:
-            if overlap:
-                _C.set_sm_reserve(0)
-
-    def _side_stream(self, dev):
-        s = getattr(self, "_comm_stream", None)
-        if s is None or s.device != dev:
-            s = self._comm_stream = torch.cuda.Stream(dev)
-        return s
 
     def _forward_overlapped(self, input_ids, positions, split: int) -> torch.Tensor:
         """Tensor-parallel forward as two micro-batches of whole sequences, A = tokens

@@ -481,3 +481,34 @@ def test_awq_gemm_workspace_size_rules():
     assert size(257, 1024, 1024) == 1024 * 1024 * 2
     assert size(20000, 384, 1024) == 0
     assert size(20000, 6144, 1024) == 6144 * 1024 * 2
+
+
+def test_awq_gemm_rows_independent_of_batch_and_sm_reserve():
+    # For more than 256 tokens a row's result must not depend on the rest of the batch or on
+    # how many SMs the persistent kernels may use: the tensor-parallel overlap runs
+    # micro-batches under an SM reserve and must equal the unsplit forward bit for bit, and
+    # a padded CUDA-graph batch must give its real rows exactly.  Shapes of the 0.6B model
+    # at TP2 (QKV N = 2048, gate_up N = 3072, o/down N = 1024).
+    for K, N, epi in [(1024, 2048, "bf16"), (1024, 3072, "silu"), (1536, 1024, "residual")]:
+        x, qw, qz, sc = _awq_case_dev(5000, K, N, seed=N)
+        if epi == "silu":
+            qw, qz, sc = _C.interleave_gate_up(qw, qz, sc)
+        qwm = _C.awq_repack(qw)
+
+        def run(rows, reserve):
+            _C.set_sm_reserve(reserve)
+            try:
+                xs = x[:rows].contiguous()
+                if epi == "residual":
+                    r = torch.zeros(rows, N, device=DEV)
+                    return _C.awq_gemm_residual(xs, qwm, qz, sc, r)
+                if epi == "silu":
+                    return _C.awq_gemm_silu(xs, qwm, qz, sc)
+                return _C.awq_gemm(xs, qwm, qz, sc)
+            finally:
+                _C.set_sm_reserve(0)
+
+        full = run(5000, 0)
+        for rows, reserve in [(5000, 16), (3000, 16), (2000, 0), (4096, 24), (777, 0)]:
+            assert torch.equal(run(rows, reserve), full[:rows]), (K, N, epi, rows, reserve)
+    assert _C.take_device_error() == 0
