@@ -563,6 +563,8 @@ def run_gemm_micro(args):
     peak_burst, _, hbm, peak_kind = peaks()
     gen = torch.Generator(device=dev).manual_seed(0)
     epi = args.gemm_epilogue
+    lines = []
+    clocks = ClockSampler(0).__enter__()   # over the whole run: one launch is too short
     for name in args.gemm_shapes.split(","):
         K, N = GEMM_SHAPES[name]
         qw, qz, sc = synthetic.random_awq(K, N, gen, dev)
@@ -587,15 +589,19 @@ def run_gemm_micro(args):
             nbytes = K * N / 2 + (K // 128) * N * 2.5 + 2 * M * K + out_bytes
             bound_tflops = min(peak_burst, flops / nbytes * hbm * 1e9 / 1e12)
             tf = flops / t / 1e12
-            print(json.dumps({
+            lines.append({
                 "metric": "AWQ W4A16 GEMM TFLOP/s", "shape": name, "epilogue": epi, "M": M,
                 "N": N, "K": K, "value": tf, "unit": "TFLOP/s", "us": t * 1e6,
                 "steps": args.steps, "frac_of_tensor_peak": tf / peak_burst,
                 "bound": "tensor" if bound_tflops >= peak_burst else "hbm",
                 "frac_of_bound": tf / bound_tflops, "peak_kind": f"{peak_kind} bf16 burst",
                 "weight_panel": bool(_C.lib().mes_awq_gemm_workspace_size(M, N, K)),
-                "l2": COLD_L2}), flush=True)
+                "l2": COLD_L2})
             del x, y
+    clocks.__exit__()
+    for line in lines:
+        line["clocks"] = clocks.summary()
+        print(json.dumps(line), flush=True)
 
 
 def run_elementwise_micro(args):
@@ -643,14 +649,19 @@ def run_elementwise_micro(args):
         ("last token + L2 (20 rows)", lambda: _C.last_token_l2(out, last), 20 * H * 2 + 20 * H * 4),
         ("varlen schedule (20 sequences)", lambda: _C.varlen_schedule(pos), T * 8 + 4 * (T + 1)),
     ]
-    for name, fn, nbytes in cases:
-        t = cold_launch_time(fn, args, dev)
-        gbs = nbytes / t / 1e9
-        print(json.dumps({
-            "metric": "HBM GB/s (algorithmic bytes)", "kernel": name, "value": gbs,
-            "unit": "GB/s", "us": t * 1e6, "bytes": nbytes, "steps": args.steps,
-            "frac_of_hbm_peak": gbs / hbm, "peak": hbm, "peak_kind": f"{peak_kind} HBM copy",
-            "l2": COLD_L2}), flush=True)
+    lines = []
+    with ClockSampler(0) as clocks:     # over all cases: one launch is too short to sample
+        for name, fn, nbytes in cases:
+            t = cold_launch_time(fn, args, dev)
+            gbs = nbytes / t / 1e9
+            lines.append({
+                "metric": "HBM GB/s (algorithmic bytes)", "kernel": name, "value": gbs,
+                "unit": "GB/s", "us": t * 1e6, "bytes": nbytes, "steps": args.steps,
+                "frac_of_hbm_peak": gbs / hbm, "peak": hbm, "peak_kind": f"{peak_kind} HBM copy",
+                "l2": COLD_L2})
+    for line in lines:
+        line["clocks"] = clocks.summary()
+        print(json.dumps(line), flush=True)
     if _C.take_device_error():
         raise RuntimeError("device error in the elementwise benchmark")
 
