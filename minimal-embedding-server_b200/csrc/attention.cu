@@ -422,7 +422,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
 varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
                              __nv_bfloat16* __restrict__ out, const int* __restrict__ hdr,
                              const int* __restrict__ cu, const int2* __restrict__ items, int Hq,
-                             int Hkv, float scale_log2, int l2_hints, int prefetch) {
+                             int Hkv, float scale_log2, int l2_hints) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -507,36 +507,9 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
         for (int c = 0; c < 4; ++c)
           load(qs + c * (kQBytes / 2), q_full, h0 * kD + c * 64, q0, pol_q);
         const int kcol = (Hq + g) * kD, vcol = (Hq + Hkv + g) * kD;
-        if (prefetch) {
-          // The next item's Q tiles and first K/V tiles into L2 now, so that its loads, issued
-          // only when this item's last S MMA frees Q, find them there.
-          const int wn = snake(n_item + 1, blockIdx.x, gridDim.x);
-          if (wn < num_work) {
-            const int2 itn = items[wn / npairs];
-            const int hn = 2 * (wn % npairs), gn = hn / rep;
-            const int sn = cu[itn.x];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) mes::tma_prefetch_2d(&map_qkv, hn * kD + c * 64, sn + itn.y * kTile);
-            for (int jn = 0; jn < 2 && jn <= itn.y; ++jn)
-#pragma unroll
-              for (int c = 0; c < 2; ++c) {
-                mes::tma_prefetch_2d(&map_qkv, (Hq + gn) * kD + c * 64, sn + jn * kTile);
-                mes::tma_prefetch_2d(&map_qkv, (Hq + Hkv + gn) * kD + c * 64, sn + jn * kTile);
-              }
-          }
-        }
         for (int j = 0; j <= it.y; ++j) {
           const int k0 = start + j * kTile;
           const int ks_ = kt % kKVStages, vs_ = vt % kKVStages;
-          if (prefetch && j + kKVStages <= it.y) {
-            // K/V tiles two stages ahead into L2: the ring holds only two of each.
-            const int kp = start + (j + kKVStages) * kTile;
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              mes::tma_prefetch_2d(&map_qkv, kcol + c * 64, kp);
-              mes::tma_prefetch_2d(&map_qkv, vcol + c * 64, kp);
-            }
-          }
           if (kt >= kKVStages &&
               !mes::mbar_wait(&k_empty[ks_], ((kt / kKVStages) & 1) ^ 1, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) {
             ok = false;
@@ -831,16 +804,6 @@ static int l2_hints() {
   return v;
 }
 
-// L2 prefetch of the next item's Q and first K/V tiles and of K/V tiles two stages ahead
-// in the head-pair kernel; MES_ATTN_PREFETCH=0 turns it off for measurements.
-static int l2_prefetch() {
-  static const int v = [] {
-    const char* e = getenv("MES_ATTN_PREFETCH");
-    return (e && atoi(e) == 0) ? 0 : 1;
-  }();
-  return v;
-}
-
 // The head-pair kernel's register split must fit in what each SM sub-partition holds for
 // the CTA at launch: three warps per sub-partition, one of them shrinking.
 template <typename K>
@@ -890,7 +853,7 @@ extern "C" int mes_varlen_attention(const void* qkv, int64_t ld, void* out, cons
     if (st != MES_OK) return st;
     kern<<<grid, kPThreads, kPSmem, s>>>(map, (__nv_bfloat16*)out, (const int*)ws,
                                          (const int*)(ws + 256), (const int2*)(ws + items_off),
-                                         Hq, Hkv, scale_log2, l2_hints(), l2_prefetch());
+                                         Hq, Hkv, scale_log2, l2_hints());
     return mes_host::from_cuda(cudaGetLastError());
   }
   static std::atomic<uint64_t> attr_done1{0};

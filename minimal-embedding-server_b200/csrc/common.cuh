@@ -167,14 +167,6 @@ __device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* m
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
-// Bring a 2-D tile of the tensor into L2 ahead of its load (a hint; nothing is written to
-// shared memory and no barrier is involved).
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
-}
 // 2-D tile load into this CTA's shared memory whose completion is counted on a barrier of
 // either CTA of the pair (cluster address from mapa_shared).
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map,

@@ -172,7 +172,7 @@ def _tp2_rank(rank, port, q):
             q.put(got)
     finally:
         if worker is not None:
-            worker._graphs.clear()
+            worker.release_graphs()
         torch.cuda.synchronize()
         dist.destroy_process_group()
 
