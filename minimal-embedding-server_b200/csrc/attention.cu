@@ -742,22 +742,34 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
       const bool valid = row_in_seq < len;
       const float inv = 1.0f / l;
       uint4* dst = reinterpret_cast<uint4*>(out + ((int64_t)(start + row_in_seq) * Hq + h) * kD);
-#pragma unroll 1
-      for (int c = 0; c < kD; c += 32) {
-        uint32_t v[32];
-        mes::tmem_ld32(t_o + c, v);
-        mes::tmem_wait_ld();
-        if (valid) {
+      // Two 32-column buffers: the load of the next chunk is in flight while the current
+      // one is scaled and stored, so only the first load's latency is exposed.
+      auto store_chunk = [&](const uint32_t (&v)[32], int c) {
+        if (!valid) return;
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 o;
-            o.x = mes::pack_bf16x2(__uint_as_float(v[i + 0]) * inv, __uint_as_float(v[i + 1]) * inv);
-            o.y = mes::pack_bf16x2(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
-            o.z = mes::pack_bf16x2(__uint_as_float(v[i + 4]) * inv, __uint_as_float(v[i + 5]) * inv);
-            o.w = mes::pack_bf16x2(__uint_as_float(v[i + 6]) * inv, __uint_as_float(v[i + 7]) * inv);
-            dst[(c + i) / 8] = o;
-          }
+        for (int i = 0; i < 32; i += 8) {
+          uint4 o;
+          o.x = mes::pack_bf16x2(__uint_as_float(v[i + 0]) * inv, __uint_as_float(v[i + 1]) * inv);
+          o.y = mes::pack_bf16x2(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
+          o.z = mes::pack_bf16x2(__uint_as_float(v[i + 4]) * inv, __uint_as_float(v[i + 5]) * inv);
+          o.w = mes::pack_bf16x2(__uint_as_float(v[i + 6]) * inv, __uint_as_float(v[i + 7]) * inv);
+          dst[(c + i) / 8] = o;
         }
+      };
+      {
+        uint32_t v0[32], v1[32];
+        mes::tmem_ld32(t_o + 0, v0);
+        mes::tmem_wait_ld();
+        mes::tmem_ld32(t_o + 32, v1);
+        store_chunk(v0, 0);
+        mes::tmem_wait_ld();
+        mes::tmem_ld32(t_o + 64, v0);
+        store_chunk(v1, 32);
+        mes::tmem_wait_ld();
+        mes::tmem_ld32(t_o + 96, v1);
+        store_chunk(v0, 64);
+        mes::tmem_wait_ld();
+        store_chunk(v1, 96);
       }
       mes::tc_fence_before();
     }
