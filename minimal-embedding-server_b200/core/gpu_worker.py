@@ -48,9 +48,9 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-from .. import _C
 from ..models.qwen2 import DecoderModel
 from ..models.registry import get_model_class
+from ..ultils.pool import last_token_l2
 
 PAD_SEQ = 128   # longest dummy sequence used for padding
 
@@ -297,7 +297,7 @@ class GPUWorker:
     def postprocess(self, outputs: torch.Tensor, last_token_indices) -> torch.Tensor:
         """fp32 ``[B, H]`` host tensor of L2-normalised last-token states."""
         idx = self._to_device(torch.as_tensor(np.asarray(last_token_indices), dtype=torch.int64))
-        emb = _C.last_token_l2(outputs, idx)
+        emb = last_token_l2(outputs, idx)
         host = torch.empty(emb.shape, dtype=torch.float32, pin_memory=True)
         host.copy_(emb, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()

@@ -226,91 +226,6 @@ qknorm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, const int64_t* _
   }
 }
 
-// Streaming variant: 8 threads per (token, head) unit, units token-major; a persistent grid
-// strides over the units, and each thread loads its next unit's two 16-byte slices before it
-// normalises and rotates the current one, so the loads of one unit overlap the arithmetic of
-// the previous (the grouped kernel above instead keeps 8 heads of loads in flight and then
-// computes, which leaves the memory system idle during its arithmetic).  Same arithmetic.
-template <bool kNorm, bool kF32Cache>
-__global__ void __launch_bounds__(256, 3)
-qknorm_rope_stream_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld,
-                          const int64_t* __restrict__ pos, const void* __restrict__ cos_sin,
-                          int64_t max_pos, const uint4* __restrict__ qw,
-                          const uint4* __restrict__ kw, int T, int Hq, int Hkv, float eps) {
-  const int nh = Hq + Hkv;
-  const int64_t units = (int64_t)T * nh;
-  const int j = threadIdx.x & 7;
-  const int64_t stride = (int64_t)gridDim.x * 32;
-  // Lanes of a warp move in lockstep (the same stride), so the shuffles below always see
-  // all 32 lanes; units past the end compute on zeros and store nothing.
-  int64_t u = (int64_t)blockIdx.x * 32 + (threadIdx.x >> 3);
-  const int64_t first = (int64_t)blockIdx.x * 32 + ((threadIdx.x >> 5) << 2);
-  uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
-  int64_t t = 0;
-  int h = 0;
-  auto fetch = [&](int64_t uu, uint4& a, uint4& b, int64_t& tt, int& hh) {
-    if (uu < units) {
-      tt = uu / nh;
-      hh = (int)(uu - tt * nh);
-      const uint4* row = reinterpret_cast<const uint4*>(qkv + tt * ld) + hh * 16 + j;
-      a = row[0];
-      b = row[8];
-    }
-  };
-  fetch(u, lo, hi, t, h);
-  for (int64_t base = first; base < units; base += stride, u += stride) {
-    uint4 nlo = make_uint4(0, 0, 0, 0), nhi = nlo;
-    int64_t nt = 0;
-    int nhd = 0;
-    fetch(u + stride, nlo, nhi, nt, nhd);
-    const bool valid = u < units;
-    int64_t ps = valid ? __ldg(pos + t) : 0;
-    if (ps < 0 || ps >= max_pos) {
-      if (valid && j == 0 && h == 0) atomicCAS(&g_err_elementwise, 0, MES_ERR_INVALID);
-      ps = 0;
-    }
-    float c[8], sn[8];
-    load_cos_sin<kF32Cache>(cos_sin, ps, j * 8, c, sn);
-    float a[8], b[8];
-    unpack8(lo, a);
-    unpack8(hi, b);
-    if (kNorm) {
-      float ss = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ss += a[i] * a[i];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ss += b[i] * b[i];
-#pragma unroll
-      for (int o = kRopeThreads / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float rs = rsqrtf(ss * (1.0f / 128.0f) + eps);
-      const uint4* w = h < Hq ? qw : kw;
-      float wa[8], wb[8];
-      unpack8(valid ? __ldg(w + j) : make_uint4(0, 0, 0, 0), wa);
-      unpack8(valid ? __ldg(w + 8 + j) : make_uint4(0, 0, 0, 0), wb);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        a[i] = round_bf16(round_bf16(a[i] * rs) * wa[i]);
-        b[i] = round_bf16(round_bf16(b[i] * rs) * wb[i]);
-      }
-    }
-    float oa[8], ob[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      oa[i] = a[i] * c[i] - b[i] * sn[i];
-      ob[i] = b[i] * c[i] + a[i] * sn[i];
-    }
-    if (valid) {
-      uint4* row = reinterpret_cast<uint4*>(qkv + t * ld) + h * 16 + j;
-      row[0] = pack8(oa);
-      row[8] = pack8(ob);
-    }
-    lo = nlo;
-    hi = nhi;
-    t = nt;
-    h = nhd;
-  }
-}
-
 // ------------------------------------ SiLU-and-mul -------------------------------------
 __global__ void silu_mul_kernel(const uint4* __restrict__ x, uint4* __restrict__ y,
                                 int64_t rows, int64_t iv) {
@@ -549,16 +464,6 @@ extern "C" int mes_add_rmsnorm_f32res(const void* x, float* residual, const void
                                                     stream);
 }
 
-// Which q/k norm + RoPE kernel runs: MES_ROPE_STREAM=1 (read once) selects the streaming
-// variant, for measurements against the grouped one.
-static bool rope_stream() {
-  static const bool v = [] {
-    const char* e = getenv("MES_ROPE_STREAM");
-    return e && atoi(e) == 1;
-  }();
-  return v;
-}
-
 extern "C" int mes_qknorm_rope(void* qkv, int64_t ld, const int64_t* positions,
                                const void* cos_sin, int cos_sin_f32, int64_t max_pos,
                                const void* q_w, const void* k_w, int64_t T, int Hq, int Hkv,
@@ -577,24 +482,7 @@ extern "C" int mes_qknorm_rope(void* qkv, int64_t ld, const int64_t* positions,
   __nv_bfloat16* p = (__nv_bfloat16*)qkv;
   const uint4* qwp = (const uint4*)q_w;
   const uint4* kwp = (const uint4*)k_w;
-  if (rope_stream()) {
-    // Persistent grid: 3 resident blocks per SM, no more blocks than 32-unit groups.
-    const int64_t groups = (T * ((int64_t)Hq + Hkv) + 31) / 32;
-    const int64_t cap = (int64_t)mes_host::sm_count() * 3;
-    const unsigned sblocks = (unsigned)(groups < cap ? groups : cap);
-    if (apply_norm) {
-      if (cos_sin_f32)
-        qknorm_rope_stream_kernel<true, true><<<sblocks, 256, 0, s>>>(p, ld, positions, cos_sin, max_pos, qwp, kwp, (int)T, Hq, Hkv, eps);
-      else
-        qknorm_rope_stream_kernel<true, false><<<sblocks, 256, 0, s>>>(p, ld, positions, cos_sin, max_pos, qwp, kwp, (int)T, Hq, Hkv, eps);
-    } else {
-      if (cos_sin_f32)
-        qknorm_rope_stream_kernel<false, true><<<sblocks, 256, 0, s>>>(p, ld, positions, cos_sin, max_pos, nullptr, nullptr, (int)T, Hq, Hkv, eps);
-      else
-        qknorm_rope_stream_kernel<false, false><<<sblocks, 256, 0, s>>>(p, ld, positions, cos_sin, max_pos, nullptr, nullptr, (int)T, Hq, Hkv, eps);
-    }
-    return mes_host::from_cuda(cudaGetLastError());
-  }
+
   if (apply_norm) {
     if (cos_sin_f32)
       qknorm_rope_kernel<true, true><<<blocks, 256, 0, s>>>(p, ld, positions, cos_sin, max_pos, qwp, kwp, (int)T, Hq, Hkv, eps);

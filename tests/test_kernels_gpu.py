@@ -172,18 +172,6 @@ def test_qknorm_rope(norm, f32cache, T, Hq, Hkv):
     assert torch.equal(got[:, (Hq + Hkv) * D:], v)
 
 
-def test_qknorm_rope_streaming_variant():
-    # The streaming q/k norm + RoPE kernel (MES_ROPE_STREAM=1, read once per process) runs
-    # the test above in a child process: same cases, same tolerances.
-    import os, subprocess, sys
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, MES_ROPE_STREAM="1")
-    r = subprocess.run([sys.executable, "-m", "pytest", os.path.join(root, "tests", "test_kernels_gpu.py"),
-                        "-q", "-m", "gpu", "-k", "test_qknorm_rope and not streaming"],
-                       env=env, capture_output=True, text=True, timeout=300, cwd=root)
-    assert r.returncode == 0 and " passed" in r.stdout, r.stdout[-3000:] + r.stderr[-2000:]
-
-
 # ------------------------------------------------------------------------------ misc
 def test_silu_mul():
     g = torch.Generator().manual_seed(5)
