@@ -141,12 +141,33 @@ class GPUWorker:
         self._no_graph: set = set()
         self._pool = None
         self.captures = 0            # graphs captured so far (for tests and benchmarks)
+        self._staging: dict = {}     # name -> (pinned host buffer, event of its last copy)
 
     def _to_device(self, array) -> torch.Tensor:
         t = torch.from_numpy(np.ascontiguousarray(array)) if isinstance(array, np.ndarray) else array
         if t.device.type == "cpu":
             t = t.pin_memory().to(self.device, non_blocking=True)
         return t
+
+    def _upload(self, name: str, array, dst: torch.Tensor | None = None) -> torch.Tensor:
+        """Asynchronous host-to-device copy of the int64 host ``array`` into ``dst`` (a new
+        device tensor if None) through a pinned staging buffer kept per ``name``; the buffer
+        is reused once its previous copy has completed."""
+        a = np.asarray(array, dtype=np.int64).reshape(-1)
+        n = a.shape[0]
+        buf, ev = self._staging.get(name, (None, None))
+        if buf is None or buf.shape[0] < n:
+            buf = torch.empty(max(n, 4096), dtype=torch.int64, pin_memory=True)
+            ev = torch.cuda.Event()
+        else:
+            ev.synchronize()
+        buf.numpy()[:n] = a
+        if dst is None:
+            dst = torch.empty(n, dtype=torch.int64, device=self.device)
+        dst.copy_(buf[:n], non_blocking=True)
+        ev.record(torch.cuda.current_stream(self.device))
+        self._staging[name] = (buf, ev)
+        return dst
 
     # ---------------------------------------------------------------- layouts and graphs
     def layout(self, positions, exact: bool = False) -> Layout:
@@ -264,12 +285,12 @@ class GPUWorker:
                 if g is not None:
                     graph, ids_s, pos_s, rows_s, out = g
                     ids_p, pos_p = lay.pad(ids_h, pos_h)
-                    ids_s.copy_(self._to_device(ids_p), non_blocking=True)
-                    pos_s.copy_(self._to_device(pos_p), non_blocking=True)
+                    self._upload("ids", ids_p, ids_s)
+                    self._upload("positions", pos_p, pos_s)
                     if rows_mode:
                         rows = np.zeros(n_rows, dtype=np.int64)
                         rows[:len(last_token_indices)] = lay.rows(last_token_indices)
-                        rows_s.copy_(self._to_device(rows), non_blocking=True)
+                        self._upload("rows", rows, rows_s)
                     graph.replay()
                     if rows_mode:
                         return out[:len(last_token_indices)], "rows"
@@ -296,12 +317,19 @@ class GPUWorker:
     @torch.no_grad()
     def postprocess(self, outputs: torch.Tensor, last_token_indices) -> torch.Tensor:
         """fp32 ``[B, H]`` host tensor of L2-normalised last-token states."""
-        idx = self._to_device(torch.as_tensor(np.asarray(last_token_indices), dtype=torch.int64))
+        idx = last_token_indices
+        if not (isinstance(idx, torch.Tensor) and idx.is_cuda):
+            idx = self._upload("last", idx.numpy() if isinstance(idx, torch.Tensor) else idx)
         emb = last_token_l2(outputs, idx)
-        host = torch.empty(emb.shape, dtype=torch.float32, pin_memory=True)
+        # One pinned result buffer, reused: the caller gets a copy of it.
+        out = getattr(self, "_host_out", None)
+        if out is None or out.numel() < emb.numel():
+            out = self._host_out = torch.empty(max(emb.numel(), 1 << 16), dtype=torch.float32,
+                                               pin_memory=True)
+        host = out[:emb.numel()].view(emb.shape)
         host.copy_(emb, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
-        return host
+        return host.clone()
 
     def embed(self, input_ids, positions, last_token_indices) -> torch.Tensor:
         """fp32 ``[B, H]`` embeddings: ``_inference`` + ``postprocess`` (the engine's call
