@@ -245,6 +245,18 @@ def test_embedding_f32_exact():
     assert got.dtype == torch.float32 and torch.equal(got, table[ids].float())
 
 
+def test_embedding_many_rows_grid_stride():
+    # More rows than one wave of warps holds (one warp per row, 8 rows per block, at most
+    # 32 blocks per SM launched), with a 16-vector row so most lanes are idle.
+    g = torch.Generator().manual_seed(18)
+    table = bf16(torch.randn(100, 128, generator=g))
+    ids = torch.randint(0, 100, (60000,), generator=g)
+    got = _C.embedding_f32(ids.to(DEV), table.to(DEV)).cpu()
+    assert torch.equal(got, table[ids].float())
+    assert torch.equal(_C.embedding(ids.to(DEV), table.to(DEV)).cpu(), table[ids])
+    assert _C.take_device_error() == 0
+
+
 def test_rmsnorm_f32_and_add_rmsnorm_f32res():
     g = torch.Generator().manual_seed(17)
     rows, H = 257, 1024
