@@ -128,8 +128,11 @@ __global__ void rmsnorm_kernel(const XT* x, const RT* residual, const uint4* __r
 // shuffles.  The token's cos/sin values (one set serves both halves) and the norm weights are
 // loaded once per group, and the group's head loads are all in flight together
 // (2 x kGroupHeads x 16 bytes per thread).  Units are token-major, so a block covers
-// consecutive kilobytes of the packed qkv rows.
-constexpr int kGroupHeads = 8;
+// consecutive kilobytes of the packed qkv rows.  Two heads per unit keep the kernel at 64
+// registers and four blocks (32 warps) per SM: measured at 20000 tokens x 24 heads, 4.8 TB/s
+// against 4.5 TB/s for eight heads per unit at two blocks per SM.
+constexpr int kGroupHeads = 2;
+constexpr int kRopeMinBlocks = 4;
 constexpr int kRopeThreads = 8;  // threads per unit
 template <bool kF32Cache>
 __device__ __forceinline__ void load_cos_sin(const void* cos_sin, int64_t ps, int cj, float (&c)[8],
@@ -148,7 +151,7 @@ __device__ __forceinline__ void load_cos_sin(const void* cos_sin, int64_t ps, in
 }
 
 template <bool kNorm, bool kF32Cache>
-__global__ void __launch_bounds__(256, 2)
+__global__ void __launch_bounds__(256, kRopeMinBlocks)
 qknorm_rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, const int64_t* __restrict__ pos,
                    const void* __restrict__ cos_sin, int64_t max_pos, const uint4* __restrict__ qw,
                    const uint4* __restrict__ kw, int T, int Hq, int Hkv, float eps) {
