@@ -366,7 +366,11 @@ constexpr int kPOffQ = 0;                                   // Q0 | Q1, 2 x 32 K
 constexpr int kPOffK = kPOffQ + 2 * kQBytes;
 constexpr int kPOffV = kPOffK + kKVStages * kKVBytes;
 constexpr int kPOffBar = kPOffV + kKVStages * kKVBytes;
-constexpr int kPSmem = kPOffBar + 256 + 1024;
+// O staging for the TMA store of the epilogue: 4 KB per softmax warp (32 rows x 64 columns
+// bf16, 128-byte swizzle), 1024-byte aligned.
+constexpr int kPOffStage = kPOffBar + 1024;
+constexpr int kStageBytes = 32 * 64 * 2;
+constexpr int kPSmem = kPOffStage + 8 * kStageBytes + 1024;
 static_assert(kPSmem <= 232448, "shared memory");
 
 __device__ __forceinline__ uint64_t f2_bits(float2 v) {
@@ -420,6 +424,7 @@ __device__ __forceinline__ int snake(int k, int b, int G) {
 template <int kPolyPairs>
 __global__ void __launch_bounds__(kPThreads, 1)
 varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
+                             const __grid_constant__ CUtensorMap map_out,
                              __nv_bfloat16* __restrict__ out, const int* __restrict__ hdr,
                              const int* __restrict__ cu, const int2* __restrict__ items, int Hq,
                              int Hkv, float scale_log2, int l2_hints) {
@@ -442,6 +447,7 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
   uint64_t* drain = bars + 16;    // abort path: issued MMAs completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* turn = bars + 18;     // [2] softmax warpgroup b may run its exp2 phase
 
   const int warp = mes::warp_id(), lane = mes::lane_id();
   const int npairs = Hq / 2;
@@ -461,12 +467,16 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
       mes::mbar_init(&s_full[b], 1);
       mes::mbar_init(&p_full[b], 4);
       mes::mbar_init(&o_full[b], 1);
+      mes::mbar_init(&turn[b], 4);
     }
     mes::mbar_init(drain, 1);
     *abort_flag = 0;
     mes::fence_barrier_init();
   }
-  if (warp == 8 && lane == 0) mes::tma_prefetch_desc(&map_qkv);
+  if (warp == 8 && lane == 0) {
+    mes::tma_prefetch_desc(&map_qkv);
+    mes::tma_prefetch_desc(&map_out);
+  }
   if (warp == 9) {
     __syncwarp();
     mes::tmem_alloc(tmem_slot, kTmemCols);
@@ -638,6 +648,7 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
     const float2 sc2 = make_float2(scale_log2, scale_log2);
     int n_item = 0, pt = 0;
     bool ok = true;
+    bool o_stored = false;  // this warp has TMA stores of O in flight
     for (int w = blockIdx.x; w < num_work && ok; w = snake(++n_item, blockIdx.x, gridDim.x)) {
       const int2 item = items[w / npairs];
       const int h = 2 * (w % npairs) + b;
@@ -692,6 +703,15 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
           m = mn;
           rescale = true;
         }
+        // The exp2 phases of the two warpgroups take turns (head 0 of step pt, head 1 of
+        // step pt, head 0 of step pt + 1, ...): both would otherwise contend for the SM's
+        // exp2 unit, finish together and leave the tensor core to run both heads' MMAs while
+        // neither softmax can proceed.  Taking turns, one head's exp2 phase runs while the
+        // tensor core computes the other head's PV and next S.
+        if (b == 1 || pt > 0) {
+          const uint32_t par = b == 0 ? ((pt - 1) & 1) : (pt & 1);
+          if (!mes::mbar_wait_warp(&turn[b], par, abort_flag, &g_err_attn, MES_ERR_TIMEOUT)) { ok = false; break; }
+        }
         const float2 nm2 = make_float2(-m, -m);
         float2 sum2[4];
 #pragma unroll
@@ -715,6 +735,8 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
           }
           mes::tmem_st16(t_s + q4 * 16, pk);
         }
+        __syncwarp();
+        if (lane == 0) mes::mbar_arrive(&turn[b ^ 1]);
         const float2 s01 = fadd2(sum2[0], sum2[1]), s23 = fadd2(sum2[2], sum2[3]);
         l += (s01.x + s23.x) + (s01.y + s23.y);
         if (rescale) {
@@ -741,20 +763,55 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
       const int row_in_seq = item.y * kTile + r;
       const bool valid = row_in_seq < len;
       const float inv = 1.0f / l;
+      auto scale8 = [&](const uint32_t (&v)[32], int i) {
+        uint4 o;
+        o.x = mes::pack_bf16x2(__uint_as_float(v[i + 0]) * inv, __uint_as_float(v[i + 1]) * inv);
+        o.y = mes::pack_bf16x2(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
+        o.z = mes::pack_bf16x2(__uint_as_float(v[i + 4]) * inv, __uint_as_float(v[i + 5]) * inv);
+        o.w = mes::pack_bf16x2(__uint_as_float(v[i + 6]) * inv, __uint_as_float(v[i + 7]) * inv);
+        return o;
+      };
+      // A warp whose 32 rows all lie in the sequence stages each 64-column half of its rows
+      // in shared memory (128-byte swizzle: 16-byte chunk c of row i at c ^ (i & 7)) and
+      // writes it with one TMA store; a warp at the end of the sequence stores its valid
+      // rows directly (a TMA box would also write the next sequence's rows).
+      const int row0 = item.y * kTile + (warp & 3) * 32;
+      if (row0 + 32 <= len) {
+        uint8_t* stg = smem + kPOffStage + warp * kStageBytes;
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          uint32_t v0[32], v1[32];
+          mes::tmem_ld32(t_o + half * 64, v0);
+          mes::tmem_ld32(t_o + half * 64 + 32, v1);
+          if (o_stored) {  // the previous store must have read the staging block
+            if (lane == 0) mes::tma_store_wait_read<0>();
+            __syncwarp();
+          }
+          mes::tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) * 16)) = scale8(v0, 8 * c);
+            *reinterpret_cast<uint4*>(stg + lane * 128 + (((c + 4) ^ (lane & 7)) * 16)) = scale8(v1, 8 * c);
+          }
+          mes::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mes::tma_store_2d(&map_out, stg, h * kD + half * 64, start + row0);
+            mes::tma_store_commit();
+          }
+          __syncwarp();
+          o_stored = true;
+        }
+        mes::tc_fence_before();
+        continue;
+      }
       uint4* dst = reinterpret_cast<uint4*>(out + ((int64_t)(start + row_in_seq) * Hq + h) * kD);
       // Two 32-column buffers: the load of the next chunk is in flight while the current
       // one is scaled and stored, so only the first load's latency is exposed.
       auto store_chunk = [&](const uint32_t (&v)[32], int c) {
         if (!valid) return;
 #pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          uint4 o;
-          o.x = mes::pack_bf16x2(__uint_as_float(v[i + 0]) * inv, __uint_as_float(v[i + 1]) * inv);
-          o.y = mes::pack_bf16x2(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
-          o.z = mes::pack_bf16x2(__uint_as_float(v[i + 4]) * inv, __uint_as_float(v[i + 5]) * inv);
-          o.w = mes::pack_bf16x2(__uint_as_float(v[i + 6]) * inv, __uint_as_float(v[i + 7]) * inv);
-          dst[(c + i) / 8] = o;
-        }
+        for (int i = 0; i < 32; i += 8) dst[(c + i) / 8] = scale8(v, i);
       };
       {
         uint32_t v0[32], v1[32];
@@ -772,6 +829,10 @@ varlen_attention_pair_kernel(const __grid_constant__ CUtensorMap map_qkv,
         store_chunk(v1, 96);
       }
       mes::tc_fence_before();
+    }
+    if (o_stored) {  // the staging blocks must outlive this warp's stores
+      if (lane == 0) mes::tma_store_wait_all<0>();
+      __syncwarp();
     }
   }
 
@@ -863,7 +924,11 @@ extern "C" int mes_varlen_attention(const void* qkv, int64_t ld, void* out, cons
                  ? MES_OK : MES_ERR_CUDA;
     });
     if (st != MES_OK) return st;
-    kern<<<grid, kPThreads, kPSmem, s>>>(map, (__nv_bfloat16*)out, (const int*)ws,
+    CUtensorMap map_out;
+    if (!mes_host::make_map_2d(&map_out, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, (int64_t)Hq * kD,
+                               (int64_t)Hq * kD, 32, 64, CU_TENSOR_MAP_SWIZZLE_128B))
+      return MES_ERR_INVALID;
+    kern<<<grid, kPThreads, kPSmem, s>>>(map, map_out, (__nv_bfloat16*)out, (const int*)ws,
                                          (const int*)(ws + 256), (const int2*)(ws + items_off),
                                          Hq, Hkv, scale_log2, l2_hints());
     return mes_host::from_cuda(cudaGetLastError());
