@@ -96,16 +96,40 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """SM clock and clock-event (throttle) reasons during the timed region: NVML read every
+    20 ms from a thread, with one sample taken before the region starts and one after it
+    ends, so that even a region shorter than the period is covered (the fields are those of
+    nvidia-smi's clocks.sm, clocks.max.sm and clocks_event_reasons.*).  Falls back to
+    ``nvidia-smi -lms 200`` when NVML cannot be loaded.  Only reads; sets nothing."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_S = 0.02
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index: int):
         self.index, self.proc, self.lines = index, None, []
+        self.nvml, self.samples, self.smax = None, [], None
 
     def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = self._nvml_handle(pynvml)
+            self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            self.bits = [pynvml.nvmlClocksEventReasonHwSlowdown,
+                         pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                         pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                         pynvml.nvmlClocksEventReasonSwPowerCap]
+            self._sample()
+            self.stop = threading.Event()
+            self.t = threading.Thread(target=self._loop, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
@@ -117,11 +141,43 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _nvml_handle(self, pynvml):
+        """NVML handle of CUDA device ``index`` (NVML numbers every GPU of the host, CUDA only
+        the visible ones: match them by PCI address)."""
+        try:
+            import torch
+            p = torch.cuda.get_device_properties(self.index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _sample(self):
+        nv = self.nvml
+        sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+        reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        self.samples.append((float(sm), int(reasons)))
+
+    def _loop(self):
+        while not self.stop.wait(self.PERIOD_S):
+            try:
+                self._sample()
+            except Exception:
+                return
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def __exit__(self, *a):
+        if self.nvml is not None:
+            self.stop.set()
+            self.t.join(timeout=5)
+            try:
+                self._sample()
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -130,8 +186,12 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, smax, reasons = [], self.smax, set()
+        for clk, bits in self.samples:
+            sm.append(clk)
+            for n, bit in zip(self.NAMES, self.bits):
+                if bits & bit:
+                    reasons.add(n)
         for ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
@@ -141,11 +201,12 @@ class ClockSampler:
                 smax = float(f[2])
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
+            for n, v in zip(self.NAMES, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvml" if self.samples else "nvidia-smi"}
 
 
 CPU_SAMPLE_SEQS = 2   # sequences of the workload's batch in one CPU sample

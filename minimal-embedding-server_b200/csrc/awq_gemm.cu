@@ -833,9 +833,8 @@ template <int EPI, bool PANEL>
 struct QCfg {
   static constexpr bool kResidual = EPI == kEpiResidual, kSilu = EPI == kEpiSilu;
   static constexpr int SETS = PANEL ? 0 : 2;
-  // The residual epilogue stages nothing in shared memory, which leaves room for one more
-  // stage; the panel variant's stages have no weight words.
-  static constexpr int SST = PANEL ? (kResidual ? 7 : 6) : (kResidual ? 6 : 5);
+  // The panel variant's stages have no weight words, which leaves room for one more stage.
+  static constexpr int SST = PANEL ? 6 : 5;
   static constexpr int kDqWarps = 4 * SETS;
   static constexpr int kEpiWarps = 8;
   static constexpr int kThreads = (2 + kDqWarps + kEpiWarps) * 32;
@@ -849,12 +848,14 @@ struct QCfg {
   static constexpr int kZBytes = (kBN / 8) * 4;
   static constexpr int kWStage = PANEL ? 0 : kWBytes + 256 + 128;
   static constexpr int kChunk = kResidual ? 16 : 32;
-  static constexpr int kOutBuf = kChunk * 32 * 2;
+  // Staging per epilogue warp: a 32-feature x 32-token bf16 block, or two 32 x 16 fp32
+  // blocks for the residual's TMA reduce-add (one filling while the other is read).
+  static constexpr int kOutBuf = kResidual ? 2 * kChunk * 32 * 4 : kChunk * 32 * 2;
   static constexpr int kOffX = 0;
   static constexpr int kOffA = SST * kXStage;
   static constexpr int kOffW = kOffA + SST * kAStage;
   static constexpr int kOffOut = kOffW + SST * kWStage;
-  static constexpr int kOffBar = kOffOut + (kResidual ? 0 : kEpiWarps * kOutBuf);
+  static constexpr int kOffBar = kOffOut + kEpiWarps * kOutBuf;
   static constexpr int kSmem = kOffBar + 512 + 1024;
   static_assert(kSmem <= 232448, "shared memory budget");
   static_assert((4 * SST + 5) * 8 + 8 <= 512, "barrier area");
@@ -899,7 +900,7 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
                      const __grid_constant__ CUtensorMap map_z,
                      const __grid_constant__ CUtensorMap map_y,
                      const __nv_bfloat16* __restrict__ bias, float* __restrict__ R, int64_t ldr,
-                     int M, int N, int K, int band, int full, int num_items) {
+                     int M, int N, int K, int band, int full, int num_items, int res_tma) {
   using C = QCfg<EPI, PANEL>;
   constexpr int SST = C::SST;
   constexpr uint32_t kTmemCols = 512;
@@ -950,7 +951,7 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
       mes::tma_prefetch_desc(&map_s);
       mes::tma_prefetch_desc(&map_z);
     }
-    if (EPI != kEpiResidual) mes::tma_prefetch_desc(&map_y);
+    if (EPI != kEpiResidual || res_tma) mes::tma_prefetch_desc(&map_y);
   }
   if (warp == 1) {
     __syncwarp();
@@ -1112,6 +1113,7 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
     const uint32_t acc_empty0 = mes::mapa_shared(mes::smem_u32(acc_empty), 0);
     __nv_bfloat16* buf = outbuf + (warp - 2 - C::kDqWarps) * (C::kOutBuf / 2);
     bool stored = false;
+    int nchunk = 0;  // residual chunks handed to TMA reduce-adds by this warp
     int lt = 0;
     for (int item = pair; item < num_items; item += npairs, ++lt) {
       const int b = lt & 1;
@@ -1133,14 +1135,36 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
         if constexpr (C::kSilu) {
           silu_chunk<C::kChunk>(v, lane, buf, stored, &map_y, n0 / 2 + q * 16, t0 + c0);
         } else if constexpr (C::kResidual) {
-          const int rows = min(C::kChunk, M - (t0 + c0));
-          float* rp = R + (int64_t)(t0 + c0) * ldr + n;
-          float rv[C::kChunk];
+          if (res_tma) {
+            // acc + bias goes to a staging block; a TMA reduce-add adds it into R in L2, so
+            // the epilogue never waits on R's loads.  Each element of R gets one fp32 add
+            // (R + (acc + bias), rounded once), as in the register path below.  Rows past M
+            // are clipped by the tensor map.
+            float* stg = reinterpret_cast<float*>(buf) + (nchunk & 1) * (C::kChunk * 32);
+            if (nchunk >= 2) {  // the reduce that last read this block must be done reading
+              if (lane == 0) mes::tma_store_wait_read<1>();
+              __syncwarp();
+            }
 #pragma unroll
-          for (int j = 0; j < C::kChunk; ++j) rv[j] = j < rows ? rp[(int64_t)j * ldr] : 0.f;
+            for (int j = 0; j < C::kChunk; ++j) stg[j * 32 + lane] = __uint_as_float(v[j]) + bv;
+            mes::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              mes::tma_reduce_add_2d(&map_y, stg, n0 + q * 32, t0 + c0);
+              mes::tma_store_commit();
+            }
+            __syncwarp();
+            ++nchunk;
+          } else {
+            const int rows = min(C::kChunk, M - (t0 + c0));
+            float* rp = R + (int64_t)(t0 + c0) * ldr + n;
+            float rv[C::kChunk];
 #pragma unroll
-          for (int j = 0; j < C::kChunk; ++j)
-            if (j < rows) rp[(int64_t)j * ldr] = rv[j] + (__uint_as_float(v[j]) + bv);
+            for (int j = 0; j < C::kChunk; ++j) rv[j] = j < rows ? rp[(int64_t)j * ldr] : 0.f;
+#pragma unroll
+            for (int j = 0; j < C::kChunk; ++j)
+              if (j < rows) rp[(int64_t)j * ldr] = rv[j] + (__uint_as_float(v[j]) + bv);
+          }
         } else {
           if (stored) {
             if (lane == 0) mes::tma_store_wait_read<0>();
@@ -1168,10 +1192,8 @@ awq_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
       if (lane == 0) mes::mbar_arrive_remote(acc_empty0 + 8 * b);
       __syncwarp();
     }
-    if (!C::kResidual) {
-      if (lane == 0) mes::tma_store_wait_all<0>();
-      __syncwarp();
-    }
+    if (lane == 0) mes::tma_store_wait_all<0>();  // stores / reduce-adds complete
+    __syncwarp();
   }
 
   mes::tc_fence_before();
@@ -1446,6 +1468,15 @@ int launch_gemm_pair(const void* X, int64_t ldx, const void* w, const int32_t* q
       return MES_ERR_INVALID;
   }
   if (!make_out_map(&my, mx, EPI, Y, M, N, ldy, C::kChunk)) return MES_ERR_INVALID;
+  // The residual epilogue adds into R with TMA reduce-adds when R's rows start on 16-byte
+  // boundaries (else it reads and writes R from registers).
+  int res_tma = 0;
+  if constexpr (C::kResidual) {
+    if ((reinterpret_cast<uintptr_t>(Y) & 15) == 0 && ldy % 4 == 0 &&
+        mes_host::make_map_2d(&my, Y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, M, N, ldy, C::kChunk, 32,
+                              CU_TENSOR_MAP_SWIZZLE_NONE))
+      res_tma = 1;
+  }
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1491,7 +1522,7 @@ int launch_gemm_pair(const void* X, int64_t ldx, const void* w, const int32_t* q
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mx, mw, ms, mz, my, (const __nv_bfloat16*)bias,
                          C::kResidual || C::kSilu ? (float*)Y : nullptr, ldy, (int)M, (int)N, (int)K,
-                         (int)band, (int)full, (int)items);
+                         (int)band, (int)full, (int)items, res_tma);
   if (e != cudaSuccess) return MES_ERR_CUDA;
   return mes_host::from_cuda(cudaGetLastError());
 }

@@ -185,6 +185,16 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
       "r"(smem_u32(src)), "r"(x), "r"(y)
       : "memory");
 }
+// R[y.., x..] += the fp32 tile at `src` (the add happens in L2; one group per call, like a
+// store: commit, then wait on the group before the tile is written again).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x,
+                                                  int y) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y)
+      : "memory");
+}
 __device__ __forceinline__ void tma_store_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
