@@ -485,6 +485,28 @@ def test_awq_gemm_panel_equals_fused(M, K, N):
         assert (a - b).abs().max().item() <= 1e-2 * b.abs().max().item()
 
 
+@pytest.mark.parametrize("M,K,N", [(257, 1024, 512), (2000, 2048, 1024)])
+def test_awq_gemm_residual_reduce_add_equals_register_path(M, K, N):
+    # A 16-byte-aligned residual with rows a multiple of 4 floats apart is updated by TMA
+    # reduce-adds in L2; any other layout by the epilogue's own read-modify-write.  Both add
+    # acc + bias to R once in fp32, so the results must agree bit for bit.
+    x, qw, qz, sc = _awq_case_dev(M, K, N, seed=M + 7)
+    qwm = _C.awq_repack(qw)
+    g = torch.Generator().manual_seed(M)
+    r0 = torch.randn(M, N, generator=g).to(DEV)
+    b = (0.1 * torch.randn(N, generator=g)).to(torch.bfloat16).to(DEV)
+    aligned = r0.clone()
+    _C.awq_gemm_residual(x, qwm, qz, sc, aligned, b)
+    strided = torch.zeros(M, N + 1, device=DEV)[:, :N]   # rows N + 1 floats apart
+    strided.copy_(r0)
+    _C.awq_gemm_residual(x, qwm, qz, sc, strided, b)
+    assert _C.take_device_error() == 0
+    assert torch.equal(aligned, strided)
+    w = _C.awq_dequant(qwm, qz, sc).float()              # W^T [N, K]
+    want = r0 + (x.float() @ w.t() + b.float())
+    assert (aligned - want).abs().max().item() <= 1e-4 * want.abs().max().item()
+
+
 def test_awq_gemm_workspace_size_rules():
     # The panel path serves batches of more than 256 tokens whose N is a multiple of 256;
     # everything else reports 0 (the fused kernels need no workspace).
