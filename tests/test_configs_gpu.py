@@ -4,7 +4,7 @@ reference's own model code on the CPU (``tests/golden/make_golden.py``).
 Each fixture holds, for one configuration's seeded AWQ checkpoint (codes and zero-points
 uniform in [0, 15], fp16 scales uniform in [0.002, 0.02]) and batch:
   * ``emb_fp32``: the reference's forward in fp32 on the exactly dequantised weights - the
-    "fp32 dequantised reference" the embeddings are judged against;
+    "fp32 dequantised reference" the embeddings are compared with;
   * ``emb_bf16``: the reference's forward in bf16 (its deployment dtype) on the same
     weights - its own distance from fp32 is the yardstick for ours;
   * checksums of every checkpoint tensor, so the test proves it regenerated the same
