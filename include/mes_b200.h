@@ -238,7 +238,9 @@ int mes_awq_gemm_residual(const void* X, int64_t ldx, const int32_t* qweight_mes
  * With a workspace of at least mes_awq_gemm_workspace_size(M, N, K) bytes (16-byte
  * aligned), large batches first dequantise the weights once into a bf16 panel W^T [N, K]
  * held there (same exact dequantisation) and then run the tensor-core mainloop on that
- * panel, instead of dequantising again in every token tile.  A NULL or smaller workspace
+ * panel, instead of dequantising again in every token tile.  Batches of 257 to 1024
+ * tokens need no workspace (the size is 0): they run the dequantising CTA-pair kernel,
+ * whose rows equal the panel path's bit for bit.  A NULL or smaller workspace otherwise
  * runs the fused kernels of the three entry points above.  The workspace is scratch:
  * its contents are undefined after the call. */
 int64_t mes_awq_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
@@ -260,7 +262,7 @@ int mes_awq_panels(int count, const int32_t* const* qweight_mes, const int32_t* 
 
 /* The GEMM of mes_awq_gemm_ws (same `epilogue` codes, Y and bias conventions) with its
  * weights given as a prepared panel (mes_awq_panels) instead of AWQ tensors.  Only for
- * shapes that take the panel path: mes_awq_gemm_workspace_size(M, N, K) > 0 (M > 256,
+ * shapes that take the panel path: mes_awq_gemm_workspace_size(M, N, K) > 0 (M > 1024,
  * N % 256 == 0); otherwise MES_ERR_INVALID.  Replaces the same projections
  * (layers/linear.py:90-180). */
 int mes_awq_gemm_on_panel(int epilogue, const void* X, int64_t ldx, const void* panel,

@@ -314,7 +314,7 @@ use_gemm_workspace = True
 
 
 def gemm_uses_panel(M: int, N: int, K: int) -> bool:
-    """Whether a GEMM of this shape runs on a dequantised weight panel (M > 256 tokens,
+    """Whether a GEMM of this shape runs on a dequantised weight panel (M > 1024 tokens,
     N % 256 == 0), when the wrappers use workspaces at all."""
     return use_gemm_workspace and int(lib().mes_awq_gemm_workspace_size(M, N, K)) > 0
 

@@ -1566,12 +1566,17 @@ int launch_panel(const int32_t* qw, const int32_t* qzeros, const void* scales, i
 // more than 256 tokens (the batches the persistent kernels serve), N a multiple of the pair
 // tile, and the panel grid within the launch limits.  MES_GEMM_PANEL=0 (read once) turns
 // the path off, for comparisons.
+// Batches above this many tokens run on a weight panel (when the caller gives a workspace);
+// up to it, the dequantising CTA-pair kernel is faster than building the panel (measured
+// per call: 0.71-0.96 of the panel path's time at 512-1024 tokens, even at 2048).
+constexpr int64_t kPanelMinTokens = 1024;
+
 bool panel_path(int64_t M, int64_t N, int64_t K) {
   static const bool enabled = [] {
     const char* v = getenv("MES_GEMM_PANEL");
     return !(v && atoi(v) == 0);
   }();
-  return enabled && M > 256 && N % (2 * kBN) == 0 && N <= (1 << 24) && K <= (1 << 24);
+  return enabled && M > kPanelMinTokens && N % (2 * kBN) == 0 && N <= (1 << 24) && K <= (1 << 24);
 }
 
 // Tile configuration for M > 64 tokens.  The environment variable MES_GEMM_CONFIG (read
@@ -1600,7 +1605,8 @@ int large_m_config() {
 template <int EPI>
 int dispatch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* qzeros,
                   const void* scales, const void* bias, void* Y, int64_t ldy, int64_t M,
-                  int64_t N, int64_t K, void* panel, int64_t panel_bytes, cudaStream_t s) {
+                  int64_t N, int64_t K, void* panel, int64_t panel_bytes, bool ws_aware,
+                  cudaStream_t s) {
   if (M <= 16) return launch_gemm<16, 16, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
   if (M <= 32) return launch_gemm<32, 11, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
   if (M <= 64) return launch_gemm<64, 7, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
@@ -1611,6 +1617,11 @@ int dispatch_gemm(const void* X, int64_t ldx, const int32_t* qw, const int32_t* 
   // each output in the same order (a row's result does not depend on the batch around it).
   if (config == 2 || (config != 1 && M <= 256 && 2 * (N / kBN) <= mes_host::persistent_ctas()))
     return launch_gemm<256, 5, 4, EPI, 8>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
+  // Mid-size batches of a workspace-aware caller (mes_awq_gemm_ws): the dequantising
+  // CTA-pair kernel, which runs the same MMAs in the same k order as the panel path above
+  // kPanelMinTokens, so a row's result does not depend on which side of it the batch is.
+  if (ws_aware && config == 0 && M > 256 && M <= kPanelMinTokens && N % (2 * kBN) == 0)
+    return launch_gemm_pair<EPI, false>(X, ldx, qw, qzeros, scales, bias, Y, ldy, M, N, K, s);
   // Large M with a workspace: dequantise the weights once into a bf16 panel, then run the
   // pair kernel on the panel, so no SM repeats the dequantisation per token tile.
   if (panel && panel_path(M, N, K) && panel_bytes >= N * K * 2) {
@@ -1686,10 +1697,15 @@ extern "C" int64_t mes_awq_gemm_workspace_size(int64_t M, int64_t N, int64_t K) 
   return panel_path(M, N, K) ? N * K * 2 : 0;
 }
 
-extern "C" int mes_awq_gemm_ws(int epilogue, const void* X, int64_t ldx, const int32_t* qweight_mes,
-                               const int32_t* qzeros, const void* scales, const void* bias, void* Y,
-                               int64_t ldy, int64_t M, int64_t N, int64_t K, int group_size,
-                               void* workspace, int64_t workspace_bytes, void* stream) {
+namespace {
+
+// The GEMM entry points.  `ws_aware`: the caller is mes_awq_gemm_ws, which sizes its
+// workspace with mes_awq_gemm_workspace_size (the three original entry points keep their
+// kernels for every M).
+int gemm_entry(int epilogue, const void* X, int64_t ldx, const int32_t* qweight_mes,
+               const int32_t* qzeros, const void* scales, const void* bias, void* Y, int64_t ldy,
+               int64_t M, int64_t N, int64_t K, int group_size, void* workspace,
+               int64_t workspace_bytes, bool ws_aware, void* stream) {
   if (epilogue < kEpiBf16 || epilogue > kEpiSilu || workspace_bytes < 0) return MES_ERR_INVALID;
   if (epilogue == kEpiSilu && bias) return MES_ERR_INVALID;
   const int st = check_gemm_args(X, ldx, qweight_mes, qzeros, scales, Y, ldy, M, N, K, group_size,
@@ -1704,37 +1720,47 @@ extern "C" int mes_awq_gemm_ws(int epilogue, const void* X, int64_t ldx, const i
   switch (epilogue) {
     case kEpiBf16:
       return dispatch_gemm<kEpiBf16>(X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K,
-                                     workspace, workspace_bytes, s);
+                                     workspace, workspace_bytes, ws_aware, s);
     case kEpiResidual:
       return dispatch_gemm<kEpiResidual>(X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N,
-                                         K, workspace, workspace_bytes, s);
+                                         K, workspace, workspace_bytes, ws_aware, s);
     default:
       return dispatch_gemm<kEpiSilu>(X, ldx, qweight_mes, qzeros, scales, nullptr, Y, ldy, M, N, K,
-                                     workspace, workspace_bytes, s);
+                                     workspace, workspace_bytes, ws_aware, s);
   }
+}
+
+}  // namespace
+
+extern "C" int mes_awq_gemm_ws(int epilogue, const void* X, int64_t ldx, const int32_t* qweight_mes,
+                               const int32_t* qzeros, const void* scales, const void* bias, void* Y,
+                               int64_t ldy, int64_t M, int64_t N, int64_t K, int group_size,
+                               void* workspace, int64_t workspace_bytes, void* stream) {
+  return gemm_entry(epilogue, X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K,
+                    group_size, workspace, workspace_bytes, true, stream);
 }
 
 extern "C" int mes_awq_gemm(const void* X, int64_t ldx, const int32_t* qweight_mes,
                             const int32_t* qzeros, const void* scales, const void* bias, void* Y,
                             int64_t ldy, int64_t M, int64_t N, int64_t K, int group_size,
                             void* stream) {
-  return mes_awq_gemm_ws(kEpiBf16, X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K,
-                         group_size, nullptr, 0, stream);
+  return gemm_entry(kEpiBf16, X, ldx, qweight_mes, qzeros, scales, bias, Y, ldy, M, N, K,
+                    group_size, nullptr, 0, false, stream);
 }
 
 extern "C" int mes_awq_gemm_residual(const void* X, int64_t ldx, const int32_t* qweight_mes,
                                      const int32_t* qzeros, const void* scales, const void* bias,
                                      float* R, int64_t ldr, int64_t M, int64_t N, int64_t K,
                                      int group_size, void* stream) {
-  return mes_awq_gemm_ws(kEpiResidual, X, ldx, qweight_mes, qzeros, scales, bias, R, ldr, M, N, K,
-                         group_size, nullptr, 0, stream);
+  return gemm_entry(kEpiResidual, X, ldx, qweight_mes, qzeros, scales, bias, R, ldr, M, N, K,
+                    group_size, nullptr, 0, false, stream);
 }
 
 extern "C" int mes_awq_gemm_silu(const void* X, int64_t ldx, const int32_t* qweight_mes,
                                  const int32_t* qzeros, const void* scales, void* Y, int64_t ldy,
                                  int64_t M, int64_t N, int64_t K, int group_size, void* stream) {
-  return mes_awq_gemm_ws(kEpiSilu, X, ldx, qweight_mes, qzeros, scales, nullptr, Y, ldy, M, N, K,
-                         group_size, nullptr, 0, stream);
+  return gemm_entry(kEpiSilu, X, ldx, qweight_mes, qzeros, scales, nullptr, Y, ldy, M, N, K,
+                    group_size, nullptr, 0, false, stream);
 }
 
 extern "C" int mes_awq_panels(int count, const int32_t* const* qweight_mes,

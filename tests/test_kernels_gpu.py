@@ -341,7 +341,7 @@ def test_awq_gemm_tile_variants(config):
     # The large-M tile variant is chosen once per process (MES_GEMM_CONFIG, MES_GEMM_PANEL),
     # so each runs in a child process: the fused dequantising kernels (0-4, weight panel
     # off) and the dequantise-once weight panel + CTA-pair kernel ("panel", the default for
-    # M > 256).  Same tolerances as test_awq_gemm_matches_fp32 and the residual test.  The
+    # M > 1024).  Same tolerances as test_awq_gemm_matches_fp32 and the residual test.  The
     # SiLU epilogue is checked against silu(x Wg) * (x Wu) in fp32 with the bf16 output
     # tolerance (it applies silu to the fp32 accumulators, one rounding at the end).
     import os, subprocess, sys
@@ -440,7 +440,7 @@ def _awq_case_dev(M, K, N, seed):
             torch.from_numpy(sc).view(torch.int16).to(DEV))
 
 
-@pytest.mark.parametrize("M,K,N", [(257, 1024, 512), (2000, 2048, 1024), (5000, 1024, 6144)])
+@pytest.mark.parametrize("M,K,N", [(1025, 1024, 512), (2000, 2048, 1024), (5000, 1024, 6144)])
 def test_awq_gemm_panel_equals_fused(M, K, N):
     # The weight panel holds the same exactly-dequantised bf16 values the fused kernels
     # build in shared memory, and the residual epilogue runs the same CTA-pair MMAs on
@@ -485,7 +485,7 @@ def test_awq_gemm_panel_equals_fused(M, K, N):
         assert (a - b).abs().max().item() <= 1e-2 * b.abs().max().item()
 
 
-@pytest.mark.parametrize("M,K,N", [(257, 1024, 512), (2000, 2048, 1024)])
+@pytest.mark.parametrize("M,K,N", [(300, 1024, 512), (2000, 2048, 1024)])
 def test_awq_gemm_residual_reduce_add_equals_register_path(M, K, N):
     # A 16-byte-aligned residual with rows a multiple of 4 floats apart is updated by TMA
     # reduce-adds in L2; any other layout by the epilogue's own read-modify-write.  Both add
@@ -508,11 +508,12 @@ def test_awq_gemm_residual_reduce_add_equals_register_path(M, K, N):
 
 
 def test_awq_gemm_workspace_size_rules():
-    # The panel path serves batches of more than 256 tokens whose N is a multiple of 256;
+    # The panel path serves batches of more than 1024 tokens whose N is a multiple of 256;
     # everything else reports 0 (the fused kernels need no workspace).
     size = _C.lib().mes_awq_gemm_workspace_size
     assert size(256, 1024, 1024) == 0
-    assert size(257, 1024, 1024) == 1024 * 1024 * 2
+    assert size(1024, 1024, 1024) == 0              # the dequantising pair kernel
+    assert size(1025, 1024, 1024) == 1024 * 1024 * 2
     assert size(20000, 384, 1024) == 0
     assert size(20000, 6144, 1024) == 6144 * 1024 * 2
 
@@ -543,6 +544,9 @@ def test_awq_gemm_rows_independent_of_batch_and_sm_reserve():
                 _C.set_sm_reserve(0)
 
         full = run(5000, 0)
-        for rows, reserve in [(5000, 16), (3000, 16), (2000, 0), (4096, 24), (777, 0)]:
+        # 1025 and more rows run on a weight panel, 257-1024 on the dequantising pair
+        # kernel: the same MMAs in the same k order.
+        for rows, reserve in [(5000, 16), (3000, 16), (2000, 0), (4096, 24), (1025, 0),
+                              (1024, 0), (777, 0), (300, 16)]:
             assert torch.equal(run(rows, reserve), full[:rows]), (K, N, epi, rows, reserve)
     assert _C.take_device_error() == 0

@@ -159,10 +159,11 @@ def test_host_argument_checks_reject_without_gpu_work():
     assert lib.mes_awq_gemm(None, 64, None, None, None, None, None, 100, 16, 100, 64, 128, None) == 1
     assert lib.mes_varlen_workspace_size(-1) == -1
     assert lib.mes_varlen_workspace_size(1000) >= 4 * 1001 + 8 * 1000
-    # GEMM weight-panel workspace: only batches of more than 256 tokens with N a multiple of
+    # GEMM weight-panel workspace: only batches of more than 1024 tokens with N a multiple of
     # the 256-feature pair tile use one; an unknown epilogue is rejected on the host.
     assert lib.mes_awq_gemm_workspace_size(256, 1024, 1024) == 0
-    assert lib.mes_awq_gemm_workspace_size(257, 1024, 1024) == 1024 * 1024 * 2
+    assert lib.mes_awq_gemm_workspace_size(1024, 1024, 1024) == 0
+    assert lib.mes_awq_gemm_workspace_size(1025, 1024, 1024) == 1024 * 1024 * 2
     assert lib.mes_awq_gemm_workspace_size(20000, 384, 1024) == 0
     assert lib.mes_awq_gemm_ws(3, None, 64, None, None, None, None, None, 64, 16, 128, 64, 128,
                                None, 0, None) == 1
