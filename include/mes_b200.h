@@ -239,7 +239,8 @@ int mes_awq_gemm_residual(const void* X, int64_t ldx, const int32_t* qweight_mes
  * aligned), large batches first dequantise the weights once into a bf16 panel W^T [N, K]
  * held there (same exact dequantisation) and then run the tensor-core mainloop on that
  * panel, instead of dequantising again in every token tile.  Batches of 257 to 1024
- * tokens need no workspace (the size is 0): they run the dequantising CTA-pair kernel,
+ * tokens need no workspace (the size is 0): they run the dequantising CTA-pair kernel (as
+ * do smaller batches too wide for the one-tile-per-CTA kernel),
  * whose rows equal the panel path's bit for bit.  A NULL or smaller workspace otherwise
  * runs the fused kernels of the three entry points above.  The workspace is scratch:
  * its contents are undefined after the call. */

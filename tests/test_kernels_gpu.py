@@ -96,7 +96,8 @@ def _gemm_case(M, K, N, bias, seed):
 @pytest.mark.parametrize("M,K,N,bias", [
     (1, 128, 128, False), (16, 256, 256, True), (17, 1024, 128, False), (64, 512, 384, True),
     (100, 1024, 256, False), (128, 256, 128, False), (129, 1024, 512, True),
-    (300, 2048, 1024, False), (1000, 1024, 6144, False), (777, 3072, 1024, True)])
+    (300, 2048, 1024, False), (1000, 1024, 6144, False), (777, 3072, 1024, True),
+    (200, 1024, 19456, True)])
 def test_awq_gemm_matches_fp32(M, K, N, bias):
     # Tolerance: fp32 accumulation order and one bf16 rounding of the output.
     y, ref = _gemm_case(M, K, N, bias, seed=M + K + N)
