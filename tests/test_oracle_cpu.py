@@ -167,8 +167,8 @@ def test_host_argument_checks_reject_without_gpu_work():
     assert lib.mes_awq_gemm_workspace_size(20000, 384, 1024) == 0
     assert lib.mes_awq_gemm_ws(3, None, 64, None, None, None, None, None, 64, 16, 128, 64, 128,
                                None, 0, None) == 1
-    assert lib.mes_awq_gemm_on_panel(0, None, 1024, None, None, None, 1024, 256, 1024, 1024,
-                                     None) == 1     # M <= 256: no panel path
+    assert lib.mes_awq_gemm_on_panel(0, None, 1024, None, None, None, 1024, 1024, 1024, 1024,
+                                     None) == 1     # M <= 1024: no panel path
     assert lib.mes_awq_panels(0, None, None, None, None, None, None, None) == 1
     assert lib.mes_wait_probe(0, 0, None) == 1             # limit out of range
     assert lib.mes_wait_probe(1_000_000_000, 0, None) == 1
@@ -177,3 +177,19 @@ def test_host_argument_checks_reject_without_gpu_work():
 def test_cpu_tensors_raise_instead_of_falling_back():
     with pytest.raises(_C.MesError):
         _C.silu_mul(torch.zeros(4, 16, dtype=torch.bfloat16))
+
+
+def test_last_token_pool_matches_oracle_post_process():
+    """``last_token_pool`` per sequence of a packed batch, then the L2 normalisation, is the
+    oracle's post-process (``ultils/pool.py:4-9``, ``core/gpu_worker.py:252-261``)."""
+    from mes_b200.ultils.pool import last_token_pool
+    g = torch.Generator().manual_seed(7)
+    lengths = [5, 1, 17, 3]
+    hidden = torch.randn(sum(lengths), 64, generator=g).to(torch.bfloat16)
+    hidden[5 + 1 - 1] = 0          # a zero row: normalised by max(||x||, 1e-12)
+    starts = np.cumsum([0] + lengths[:-1])
+    pooled = torch.stack([last_token_pool(hidden[s:s + n], n) for s, n in zip(starts, lengths)])
+    got = torch.nn.functional.normalize(pooled.float(), p=2, dim=1)
+    want = ops.last_token_l2(hidden, starts + np.array(lengths) - 1)
+    assert torch.equal(got, want)
+    assert not torch.isnan(got).any()
