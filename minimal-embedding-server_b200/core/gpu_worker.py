@@ -105,8 +105,16 @@ class Layout:
             out_pos[d0 + m:d0 + n] = np.arange(n - m) % PAD_SEQ
         return out_ids, out_pos
 
-    def rows(self, idx) -> np.ndarray:
-        """Device rows of host token indices ``idx``."""
+    def rows(self, idx):
+        """Device rows of host token indices ``idx``: a numpy array for a list or array, an
+        int64 tensor on the same device for a tensor (mapped there, without a host
+        synchronisation)."""
+        if isinstance(idx, torch.Tensor):
+            idx = idx.to(torch.int64)
+            out = idx.clone()
+            for s0, s1, d0, _ in self.parts:
+                out = torch.where((idx >= s0) & (idx < s1), idx - s0 + d0, out)
+            return out
         idx = np.asarray(idx, dtype=np.int64)
         out = idx.copy()
         for s0, s1, d0, _ in self.parts:
@@ -278,7 +286,10 @@ class GPUWorker:
             ids_h = np.asarray(input_ids.numpy() if isinstance(input_ids, torch.Tensor) else input_ids)
             pos_h = np.asarray(positions.numpy() if isinstance(positions, torch.Tensor) else positions)
             lay = self._graph_layout(pos_h)
-            rows_mode = rows_mode and lay.split == DecoderModel.NO_SPLIT
+            # The last-rows graph takes host row indices (device ones pool the full output).
+            rows_mode = (rows_mode and lay.split == DecoderModel.NO_SPLIT
+                         and not (isinstance(last_token_indices, torch.Tensor)
+                                  and last_token_indices.is_cuda))
             n_rows = -(-len(last_token_indices) // 16) * 16 if rows_mode else 0
             if (lay.key, n_rows) not in self._no_graph:
                 g = self._graph_for(lay, ids_h, pos_h, n_rows)
@@ -298,7 +309,7 @@ class GPUWorker:
         input_ids = self._to_device(input_ids).to(torch.int64)
         positions = self._to_device(positions).to(torch.int64)
         if rows_mode and (self.tp_size == 1 or self.model.model._overlap_split(positions) is None):
-            rows = self._to_device(torch.as_tensor(np.asarray(last_token_indices), dtype=torch.int64))
+            rows = self._to_device(torch.as_tensor(last_token_indices, dtype=torch.int64))
             return self.model.forward_last_rows(input_ids, positions, rows), "rows"
         return self.model(input_ids=input_ids, positions=positions), None
 

@@ -116,12 +116,17 @@ def test_last_rows_only_matches_full_forward():
         ids, pos, last = synthetic.packed_batch(lengths, cfg.vocab_size, seed=3)
         full = worker.embed(ids, pos, last).numpy()
         worker.last_rows_only = True
+        idx = torch.from_numpy(last).to("cuda:0")
         try:
             graph = worker.embed(ids, pos, last).numpy()
+            # Device indices: the full-output graph, pooled at the rows mapped on the device.
+            graph_dev = worker.embed(ids, pos, idx).numpy()
             worker.use_cuda_graphs = False
             eager = worker.embed(ids, pos, last).numpy()
+            eager_dev = worker.embed(ids, pos, idx).numpy()
         finally:
             worker.last_rows_only, worker.use_cuda_graphs = False, True
         assert np.array_equal(graph, eager), lengths
+        assert np.array_equal(graph_dev, full) and np.array_equal(eager_dev, eager), lengths
         assert _cos(graph, full).min() >= 0.99999, _cos(graph, full)
     assert _C.take_device_error() == 0

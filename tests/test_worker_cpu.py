@@ -75,6 +75,9 @@ def test_layout_pads_each_micro_batch_with_new_sequences(monkeypatch, tp, length
     for r in lay.rows(last):
         nxt = r + 1
         assert nxt == lay.total or ppos[nxt] != ppos[r] + 1
+    # Index tensors map on their own device, to the same rows.
+    got = lay.rows(torch.from_numpy(last).to(torch.int32))
+    assert got.dtype == torch.int64 and np.array_equal(got.numpy(), lay.rows(last))
 
 
 def test_exact_layout_is_unpadded():
