@@ -1,9 +1,11 @@
 """ctypes binding of ``lib/libmes_b200.so`` (the C ABI declared in ``include/mes_b200.h``).
 
-Every function here takes torch CUDA tensors, checks shapes/dtypes on the host, passes
-raw device pointers plus the current CUDA stream to the library and raises
-:class:`MesError` on a non-zero status.  There is no fallback: if the library is missing,
-fails to load, or no CUDA device is present, the call raises.
+Every function here takes torch CUDA tensors, checks on the host that each tensor whose
+pointer it passes lies on the same device and has the dtype, shape and layout the kernel
+reads (a host pointer or a short buffer would otherwise reach the GPU), passes raw device
+pointers plus the current CUDA stream to the library and raises :class:`MesError` on a
+non-zero status.  There is no fallback: if the library is missing, fails to load, or no
+CUDA device is present, the call raises.
 """
 from __future__ import annotations
 
@@ -123,6 +125,38 @@ def _need(cond: bool, msg: str) -> None:
         raise MesError(msg)
 
 
+def _arg(t, name: str, like: torch.Tensor, dtype=None, shape=None, contiguous: bool = False,
+         unit_stride: bool = False) -> None:
+    """Check the tensor argument ``t`` (None passes) before its pointer goes to a kernel: on
+    ``like``'s device, of ``dtype`` (a dtype or a tuple of them), of ``shape``, contiguous
+    or with unit inner stride when asked."""
+    if t is None:
+        return
+    if t.device != like.device:
+        raise MesError(f"{name} is on {t.device}, the kernel runs on {like.device}")
+    if dtype is not None and t.dtype not in (dtype if isinstance(dtype, tuple) else (dtype,)):
+        raise MesError(f"{name} must be {dtype}, got {t.dtype}")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise MesError(f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+    if contiguous and not t.is_contiguous():
+        raise MesError(f"{name} must be contiguous")
+    if unit_stride and t.stride(-1) != 1:
+        raise MesError(f"{name} must have unit inner stride")
+
+
+_SCALES = (torch.int16, torch.float16)   # fp16 scales, or their int16 bit pattern
+
+
+def _awq_args(qweight_mes, qzeros, scales, like: torch.Tensor, group_size: int) -> None:
+    """Kernel-layout AWQ tensors: qweight_mes i32 [K/8, N], qzeros i32 [K/G, N/8], scales
+    fp16 (or int16 bits) [K/G, N], all contiguous on ``like``'s device."""
+    _need(qweight_mes.dim() == 2 and group_size > 0, "qweight_mes must be int32 [K/8, N]")
+    K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
+    _arg(qweight_mes, "qweight_mes", like, torch.int32, contiguous=True)
+    _arg(qzeros, "qzeros", like, torch.int32, (K // group_size, N // 8), contiguous=True)
+    _arg(scales, "scales", like, _SCALES, (K // group_size, N), contiguous=True)
+
+
 def take_device_error() -> int:
     code = _i32(0)
     _check(lib().mes_take_device_error(ctypes.byref(code)), "mes_take_device_error", 0)
@@ -142,6 +176,8 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None =
     _need(table.dtype == torch.bfloat16 and table.dim() == 2 and table.is_contiguous(),
           "table must be contiguous bf16 [vocab, H]")
     T, (V, H) = ids.shape[0], table.shape
+    _arg(ids, "ids", table)
+    _arg(out, "out", table, torch.bfloat16, (T, H), contiguous=True)
     if out is None:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=table.device)
     ids = ids.contiguous()
@@ -156,6 +192,8 @@ def embedding_f32(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | No
     _need(table.dtype == torch.bfloat16 and table.dim() == 2 and table.is_contiguous(),
           "table must be contiguous bf16 [vocab, H]")
     T, (V, H) = ids.shape[0], table.shape
+    _arg(ids, "ids", table)
+    _arg(out, "out", table, torch.float32, (T, H), contiguous=True)
     if out is None:
         out = torch.empty(T, H, dtype=torch.float32, device=table.device)
     _check(lib().mes_embedding_f32(_p(ids.contiguous()), T, _p(table), V, H, _p(out),
@@ -168,6 +206,9 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | No
     _need(x.dtype in (torch.bfloat16, torch.float32) and x.is_contiguous(),
           "x must be contiguous bf16 or fp32")
     H = x.shape[-1]
+    _need(x.dim() >= 1 and H > 0, "x must be [..., H] with H > 0")
+    _arg(w, "w", x, torch.bfloat16, (H,), contiguous=True)
+    _arg(out, "out", x, torch.bfloat16, x.shape, contiguous=True)
     if out is None:
         out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
     fn = lib().mes_rmsnorm if x.dtype == torch.bfloat16 else lib().mes_rmsnorm_f32in
@@ -182,6 +223,10 @@ def add_rmsnorm_f32res(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
     _need(x.is_contiguous() and residual.is_contiguous() and x.shape == residual.shape,
           "x and residual must be contiguous and of one shape")
     H = x.shape[-1]
+    _need(x.dim() >= 1 and H > 0, "x must be [..., H] with H > 0")
+    _arg(residual, "residual", x)
+    _arg(w, "w", x, torch.bfloat16, (H,), contiguous=True)
+    _arg(out, "out", x, torch.bfloat16, x.shape, contiguous=True)
     out = torch.empty_like(x) if out is None else out
     _check(lib().mes_add_rmsnorm_f32res(_p(x), _p(residual), _p(w), _p(out), x.numel() // H, H,
                                         eps, _stream(x)), "mes_add_rmsnorm_f32res")
@@ -194,6 +239,11 @@ def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: f
     _need(x.is_contiguous() and residual.is_contiguous() and x.shape == residual.shape,
           "x and residual must be contiguous and of one shape")
     H = x.shape[-1]
+    _need(x.dim() >= 1 and H > 0, "x must be [..., H] with H > 0")
+    _arg(residual, "residual", x)
+    _arg(w, "w", x, torch.bfloat16, (H,), contiguous=True)
+    _arg(out, "out", x, torch.bfloat16, x.shape, contiguous=True)
+    _arg(residual_out, "residual_out", x, torch.bfloat16, x.shape, contiguous=True)
     out = torch.empty_like(x) if out is None else out
     residual_out = torch.empty_like(residual) if residual_out is None else residual_out
     _check(lib().mes_add_rmsnorm(_p(x), _p(residual), _p(w), _p(out), _p(residual_out),
@@ -213,6 +263,13 @@ def qknorm_rope(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tenso
     _need(cos_sin.dtype in (torch.float32, torch.bfloat16) and cos_sin.is_contiguous(),
           "cos_sin must be a contiguous fp32/bf16 cache")
     apply_norm = q_weight is not None or k_weight is not None
+    _need(positions.dim() == 1 and qkv.dim() == 2 and qkv.shape[0] == positions.shape[0],
+          "qkv must be [T, ...] for positions [T]")
+    _need(cos_sin.dim() == 2 and cos_sin.shape[1] == head_dim, "cos_sin must be [max_pos, D]")
+    _arg(positions, "positions", qkv)
+    _arg(cos_sin, "cos_sin", qkv)
+    _arg(q_weight, "q_weight", qkv, torch.bfloat16, (head_dim,), contiguous=True)
+    _arg(k_weight, "k_weight", qkv, torch.bfloat16, (head_dim,), contiguous=True)
     T = positions.shape[0]
     _check(lib().mes_qknorm_rope(_p(qkv), qkv.stride(0), _p(positions.contiguous()),
                                  _p(cos_sin), int(cos_sin.dtype == torch.float32),
@@ -226,6 +283,7 @@ def silu_mul(x: torch.Tensor, out: torch.Tensor | None = None):
     _need(x.dtype == torch.bfloat16 and x.is_contiguous() and x.shape[-1] % 2 == 0,
           "x must be contiguous bf16 [..., 2I]")
     I = x.shape[-1] // 2
+    _arg(out, "out", x, torch.bfloat16, (*x.shape[:-1], I), contiguous=True)
     if out is None:
         out = torch.empty(*x.shape[:-1], I, dtype=x.dtype, device=x.device)
     _check(lib().mes_silu_mul(_p(x), _p(out), x.numel() // (2 * I), I, _stream(x)),
@@ -243,6 +301,7 @@ def varlen_schedule(positions: torch.Tensor, workspace: torch.Tensor | None = No
     size = varlen_workspace_size(T)
     if workspace is None:
         workspace = torch.empty(size, dtype=torch.uint8, device=positions.device)
+    _arg(workspace, "workspace", positions, torch.uint8, contiguous=True)
     _need(workspace.numel() >= size, "workspace too small")
     positions = positions.contiguous()
     _check(lib().mes_varlen_schedule(_p(positions), T, _p(workspace), _stream(positions)),
@@ -251,6 +310,8 @@ def varlen_schedule(positions: torch.Tensor, workspace: torch.Tensor | None = No
 
 
 def varlen_cu_seqlens(workspace: torch.Tensor, T: int):
+    _need(workspace.dtype == torch.uint8 and workspace.numel() >= varlen_workspace_size(T),
+          "workspace must be the uint8 schedule of a batch of T tokens")
     cu = torch.empty(T + 1, dtype=torch.int32, device=workspace.device)
     n = torch.empty(1, dtype=torch.int32, device=workspace.device)
     _check(lib().mes_varlen_cu_seqlens(_p(workspace), T, _p(cu), _p(n), _stream(workspace)),
@@ -261,8 +322,12 @@ def varlen_cu_seqlens(workspace: torch.Tensor, T: int):
 def varlen_attention(qkv: torch.Tensor, workspace: torch.Tensor, num_heads: int,
                      num_kv_heads: int, head_dim: int, scale: float,
                      out: torch.Tensor | None = None):
-    _need(qkv.dtype == torch.bfloat16 and qkv.stride(-1) == 1, "qkv must be bf16, unit stride")
+    _need(qkv.dtype == torch.bfloat16 and qkv.dim() == 2 and qkv.stride(-1) == 1,
+          "qkv must be bf16 [T, (Hq + 2 Hkv) D], unit stride")
     T = qkv.shape[0]
+    _arg(workspace, "workspace", qkv, torch.uint8, contiguous=True)
+    _need(workspace.numel() >= varlen_workspace_size(T), "workspace too small for T tokens")
+    _arg(out, "out", qkv, torch.bfloat16, (T, num_heads * head_dim), contiguous=True)
     if out is None:
         out = torch.empty(T, num_heads * head_dim, dtype=torch.bfloat16, device=qkv.device)
     _check(lib().mes_varlen_attention(_p(qkv), qkv.stride(0), _p(out), _p(workspace), T,
@@ -274,9 +339,11 @@ def varlen_attention(qkv: torch.Tensor, workspace: torch.Tensor, num_heads: int,
 def last_token_l2(hidden: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = None):
     _need(hidden.dtype == torch.bfloat16 and hidden.is_contiguous() and hidden.dim() == 2,
           "hidden must be contiguous bf16 [T, H]")
-    _need(idx.dtype == torch.int64, "indices must be int64")
+    _need(idx.dtype == torch.int64 and idx.dim() == 1, "indices must be int64 [B]")
     T, H = hidden.shape
     B = idx.shape[0]
+    _arg(idx, "indices", hidden)
+    _arg(out, "out", hidden, torch.float32, (B, H), contiguous=True)
     if out is None:
         out = torch.empty(B, H, dtype=torch.float32, device=hidden.device)
     _check(lib().mes_last_token_l2(_p(hidden), T, H, _p(idx.contiguous()), B, _p(out),
@@ -296,6 +363,7 @@ def awq_repack(qweight: torch.Tensor) -> torch.Tensor:
 def awq_dequant(qweight_mes: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
                 group_size: int = 128) -> torch.Tensor:
     """bf16 W^T [N, K] with the GEMM's exact dequantisation (for verification)."""
+    _awq_args(qweight_mes, qzeros, scales, qweight_mes, group_size)
     K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
     out = torch.empty(N, K, dtype=torch.bfloat16, device=qweight_mes.device)
     _check(lib().mes_awq_dequant(_p(qweight_mes), _p(qzeros), _p(scales), K, N, group_size,
@@ -332,8 +400,9 @@ def awq_panels(weights, panels) -> None:
     K = arr([w[0].shape[0] * 8 for w in weights], _i64)
     N = arr([w[0].shape[1] for w in weights], _i64)
     for (w, p_) in zip(weights, panels):
-        _need(p_.dtype == torch.bfloat16 and p_.is_contiguous()
-              and tuple(p_.shape) == (w[0].shape[1], w[0].shape[0] * 8), "panel must be bf16 [N, K]")
+        _awq_args(*w, panels[0], 128)
+        _arg(p_, "panel", panels[0], torch.bfloat16, (w[0].shape[1], w[0].shape[0] * 8),
+             contiguous=True)
     _check(lib().mes_awq_panels(n, qw, qz, sc, K, N, arr([_p(p_) for p_ in panels], _vp),
                                 _stream(panels[0])), "mes_awq_panels")
 
@@ -341,8 +410,12 @@ def awq_panels(weights, panels) -> None:
 def _awq_gemm_call(epi: int, x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
                    scales: torch.Tensor, bias, y: torch.Tensor, group_size: int,
                    panel: torch.Tensor | None = None) -> None:
+    _awq_args(qweight_mes, qzeros, scales, x, group_size)
     K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
     M = x.shape[0]
+    _arg(bias, "bias", x, torch.bfloat16, (N,), contiguous=True)
+    _arg(y, "output", x, unit_stride=True)
+    _arg(panel, "panel", x)
     ev = gemm_events if gemm_event_kinds is None or _EPI_NAME[epi] in gemm_event_kinds else None
     if ev is not None:
         e0, e1 = _timing_event(), _timing_event()
@@ -374,7 +447,8 @@ def awq_gemm_residual(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.
     _need(residual.dtype == torch.float32 and residual.stride(-1) == 1, "fp32 residual")
     K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
     M = x.shape[0]
-    _need(x.shape[1] == K and tuple(residual.shape) == (M, N), "shape mismatch")
+    _need(x.shape[1] == K and residual.dim() == 2 and tuple(residual.shape) == (M, N),
+          "shape mismatch")
     _awq_gemm_call(EPI_RESIDUAL, x, qweight_mes, qzeros, scales, bias, residual, group_size, panel)
     return residual
 
@@ -389,6 +463,7 @@ def awq_gemm_silu(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tens
     K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
     M = x.shape[0]
     _need(x.shape[1] == K, f"x has K={x.shape[1]}, weight has K={K}")
+    _arg(out, "out", x, torch.bfloat16, (M, N // 2), unit_stride=True)
     if out is None:
         out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=x.device)
     _awq_gemm_call(EPI_SILU, x, qweight_mes, qzeros, scales, None, out, group_size, panel)
@@ -419,6 +494,7 @@ def awq_gemm(x: torch.Tensor, qweight_mes: torch.Tensor, qzeros: torch.Tensor,
     K, N = qweight_mes.shape[0] * 8, qweight_mes.shape[1]
     M = x.shape[0]
     _need(x.shape[1] == K, f"x has K={x.shape[1]}, weight has K={K}")
+    _arg(out, "out", x, torch.bfloat16, (M, N), unit_stride=True)
     if out is None:
         out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
     _awq_gemm_call(EPI_BF16, x, qweight_mes, qzeros, scales, bias, out, group_size, panel)
