@@ -1,13 +1,26 @@
 """The torch-facing wrappers' host checks, on CPU.  The library's launch entry points are
 replaced by a recorder (its size queries stay the real library's): every call the model
 makes in a forward passes the checks, and a tensor on another device, of another dtype or
-of another shape is refused before any pointer reaches the library."""
+of another shape is refused before any pointer reaches the library.  At tensor parallelism 2
+(two ``gloo`` ranks) the overlapped forward's calls pass them too."""
+import datetime
+import os
+import socket
+import sys
+
 import pytest
 import torch
+import torch.multiprocessing as mp
 
-from mes_b200 import _C, synthetic
-from mes_b200.models import Qwen2ForCausalLM, Qwen3ForCausalLM
-from mes_b200.schemas.config import MESConfig
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+import __graft_entry__  # noqa: E402  (spawned ranks import this module by name)
+
+__graft_entry__.load_package()
+
+from mes_b200 import _C, synthetic  # noqa: E402
+from mes_b200.models import Qwen2ForCausalLM, Qwen3ForCausalLM  # noqa: E402
+from mes_b200.schemas.config import MESConfig  # noqa: E402
 
 _REAL = ("mes_varlen_workspace_size", "mes_awq_gemm_workspace_size", "mes_status_string")
 
@@ -16,6 +29,7 @@ class _RecordingLib:
     def __init__(self, real):
         self.real = real
         self.calls = []
+        self.reserve = []        # values given to mes_set_sm_reserve
 
     def __getattr__(self, name):
         if name in _REAL:
@@ -23,6 +37,8 @@ class _RecordingLib:
 
         def launch(*args):
             self.calls.append(name)
+            if name == "mes_set_sm_reserve":
+                self.reserve.append(args[0])
             return 0
         return launch
 
@@ -116,3 +132,46 @@ def test_bad_arguments_are_refused_before_the_library(rec):
     _C.awq_panels([(qw, qz, sc)], [torch.empty(128, 256, dtype=torch.bfloat16)])
     assert rec.calls == ["mes_rmsnorm", "mes_qknorm_rope", "mes_varlen_attention",
                          "mes_awq_gemm_ws", "mes_awq_panels"]
+
+
+def _tp_rank(rank, world, port, q):
+    import torch.distributed as dist
+    from mes_b200.models import qwen2
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        fake = _RecordingLib(_C.lib())
+        _C.lib = lambda: fake
+        _C._stream = lambda t: 0
+        cfg = synthetic.qwen3_0_6b(num_hidden_layers=2, vocab_size=1000)
+        model = Qwen3ForCausalLM(MESConfig(model_config=cfg))
+        ids, pos, _ = synthetic.packed_batch([1000] * 5, cfg.vocab_size)
+        split = qwen2.DecoderModel.overlap_split_host(pos)
+        out = model(torch.from_numpy(ids), torch.from_numpy(pos), split)
+        q.put((rank, split, tuple(out.shape), fake.reserve, sorted(set(fake.calls))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_overlapped_forward_calls_pass_the_checks():
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_tp_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    results = [q.get(timeout=10) for _ in procs]
+    for rank, split, shape, reserve, calls in results:
+        assert split == 2000 and shape == (5000, 1024), (rank, split, shape)
+        # The persistent kernels leave 16 SMs to NCCL during the overlap, then all of them.
+        assert reserve == [16, 0], reserve
+        # Micro-batches of 2000 / 3000 tokens: panel GEMMs; the bf16 partial products are
+        # all-reduced, then added into the residual by the add + RMSNorm kernel.
+        assert {"mes_awq_panels", "mes_awq_gemm_on_panel", "mes_add_rmsnorm_f32res",
+                "mes_varlen_attention", "mes_qknorm_rope"} <= set(calls), calls
