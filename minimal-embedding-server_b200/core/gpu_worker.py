@@ -273,6 +273,12 @@ class GPUWorker:
         self._exact.clear()
 
     # ---------------------------------------------------------------- forward
+    def _hidden_size(self) -> int:
+        cfg = getattr(self.mes_config, "model_config", None)
+        if cfg is not None:
+            return int(cfg.hidden_size)
+        return int(self.model.model.embed_tokens.embedding_dim)
+
     @torch.no_grad()
     def _forward(self, input_ids, positions, last_token_indices=None):
         """Forward of one batch: ``(hidden, layout)``.  ``hidden`` holds the model output in
@@ -318,6 +324,8 @@ class GPUWorker:
         """``[T, H]`` hidden states of the batch (``gpu_worker.py:216-222``).  With CUDA
         graphs the result lives in the graph's output buffer: it is overwritten by the
         next call."""
+        if len(positions) == 0:
+            return torch.empty(0, self._hidden_size(), dtype=torch.bfloat16, device=self.device)
         out, lay = self._forward(input_ids, positions)
         if lay is None or not lay.padded:
             return out
@@ -344,7 +352,9 @@ class GPUWorker:
 
     def embed(self, input_ids, positions, last_token_indices) -> torch.Tensor:
         """fp32 ``[B, H]`` embeddings: ``_inference`` + ``postprocess`` (the engine's call
-        per batch)."""
+        per batch).  A batch without sequences gives ``[0, H]`` and launches nothing."""
+        if len(last_token_indices) == 0:
+            return torch.empty(0, self._hidden_size(), dtype=torch.float32)
         if self.last_rows_only:
             out, lay = self._forward(input_ids, positions, last_token_indices)
             if lay == "rows":

@@ -119,3 +119,19 @@ def test_padding_leaves_real_embeddings_unchanged(monkeypatch, tp, lengths):
     want = omodel.embed(cfg, W, torch.from_numpy(ids), torch.from_numpy(pos), last)
     got = omodel.embed(cfg, W, torch.from_numpy(pids), torch.from_numpy(ppos), lay.rows(last))
     torch.testing.assert_close(got, want, rtol=0, atol=1e-5)
+
+
+def test_empty_batch_launches_nothing():
+    def fail(*a, **k):
+        raise AssertionError("the model ran for an empty batch")
+    stub = types.SimpleNamespace(tp_size=1, forward_last_rows=fail)
+    stub.eval = lambda: stub
+    cfg = types.SimpleNamespace(model_config=types.SimpleNamespace(hidden_size=64))
+    w = gw.GPUWorker(cfg, device="cpu", model=stub)
+    w.model = fail
+    empty = np.zeros(0, dtype=np.int64)
+    emb = w.embed(empty, empty, [])
+    assert emb.shape == (0, 64) and emb.dtype == torch.float32
+    assert w.embed_list(empty, empty, []) == []
+    hidden = w._inference(empty, empty)
+    assert hidden.shape == (0, 64) and hidden.dtype == torch.bfloat16
