@@ -10,6 +10,9 @@ if ROOT not in sys.path:
 
 import __graft_entry__  # noqa: E402
 
+# A fresh checkout has no library yet: build it once (nvcc cross-compiles without a GPU).
+if not os.path.exists(os.path.join(__graft_entry__.PKG_DIR, "lib", "libmes_b200.so")):
+    __graft_entry__.build()
 __graft_entry__.load_package()
 
 
