@@ -297,7 +297,6 @@ def run_reference(args):
 
 # ---------------------------------------------------------------------------- GPU arm
 def run_mes(args):
-    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -670,7 +669,6 @@ def run_elementwise_micro(args):
     Qwen3-0.6B workload (T = 20000, H = 1024, 16 q / 8 kv heads of 128, I = 3072), one JSON
     line per kernel: algorithmic HBM bytes per launch / CUDA-event time, against the HBM
     peak.  Each launch is timed alone with a cold L2 (``cold_launch_time``)."""
-    import numpy as np
     import torch
     import __graft_entry__
     __graft_entry__.build()

@@ -1,6 +1,5 @@
 """CPU tests: the oracle against the reference's golden fixtures, the AWQ format against
 vLLM's packer, and the C-ABI library's exports (no GPU work)."""
-import ctypes
 import os
 import re
 
