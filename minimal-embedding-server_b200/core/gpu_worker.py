@@ -178,12 +178,14 @@ class GPUWorker:
         return dst
 
     # ---------------------------------------------------------------- layouts and graphs
-    def layout(self, positions, exact: bool = False) -> Layout:
-        """Device layout of a host batch: its micro-batch boundary (tp > 1) and, unless
+    def layout(self, positions, exact: bool = False, split: int | None = None) -> Layout:
+        """Device layout of a host batch: its micro-batch boundary (tp > 1; ``split`` when
+        the caller already has it from :meth:`DecoderModel.overlap_split_host`) and, unless
         ``exact``, each micro-batch padded to its token bucket."""
         pos = np.asarray(positions)
         T = int(pos.shape[0])
-        split = DecoderModel.overlap_split_host(pos, self.tp_size)
+        if split is None:
+            split = DecoderModel.overlap_split_host(pos, self.tp_size)
         if split == DecoderModel.NO_SPLIT:
             spans = [(0, T)]
         else:
@@ -199,10 +201,11 @@ class GPUWorker:
     def _graph_layout(self, positions) -> Layout:
         """Layout to run a host batch with: exact when its graph exists, its layout needs no
         padding, or it has now occurred ``exact_after`` times; else bucketed."""
-        exact = self.layout(positions, exact=True)
+        split = DecoderModel.overlap_split_host(np.asarray(positions), self.tp_size)
+        exact = self.layout(positions, exact=True, split=split)
         if any(k[0] == exact.key for k in self._exact):
             return exact
-        bucket = self.layout(positions)
+        bucket = self.layout(positions, split=split)
         if not bucket.padded:
             return exact
         if len(self._seen) > 4096:       # forget old shapes; the counts only pick exact graphs
