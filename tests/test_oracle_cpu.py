@@ -152,6 +152,28 @@ def test_library_loads_and_exports_every_header_symbol():
     assert _C.status_string(1) == "invalid argument or unsupported shape"
 
 
+def test_binding_signatures_mirror_the_header():
+    """Every prototype of the header has the ctypes signature ``_C`` declares: the same
+    return type and, argument by argument, a pointer, int64, int or float."""
+    import ctypes
+    text = re.sub(r"/\*.*?\*/", "", open(os.path.join(ROOT, "include", "mes_b200.h")).read(),
+                  flags=re.S)
+    protos = re.findall(r"^(int|int64_t|const char\*)\s+(mes_\w+)\(([^;]*?)\);", text, re.M | re.S)
+    assert len(protos) == len(_header_functions())
+    ret_kind = {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "const char*": ctypes.c_char_p}
+    arg_kind = {ctypes.c_void_p: "ptr", ctypes.c_int64: "int64_t", ctypes.c_int: "int",
+                ctypes.c_float: "float"}
+    for ret, name, params in protos:
+        want = []
+        for prm in params.split(","):
+            prm = " ".join(prm.split())
+            if prm and prm != "void":
+                want.append("ptr" if "*" in prm else prm.rsplit(" ", 1)[0])
+        res, args = _C.SIGNATURES[name]
+        assert res is ret_kind[ret], name
+        assert [arg_kind.get(a, "ptr") for a in args] == want, name
+
+
 def test_host_argument_checks_reject_without_gpu_work():
     lib = _C.lib()
     # N not a multiple of 128 -> MES_ERR_INVALID before any CUDA call
