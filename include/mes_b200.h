@@ -12,6 +12,11 @@
  *   - The return value is a mes_status (0 = success).  Argument errors are detected on
  *     the host before anything is launched.  Device-side wait limits record a code that
  *     mes_take_device_error() returns.
+ *   - Alignment: activation, weight, scale/zero-point and output arrays start on 16-byte
+ *     boundaries (the kernels move them with TMA or as 16-byte vectors); index arrays
+ *     (i64 ids, positions, row indices) on 8 bytes; the f32 residual R of
+ *     mes_awq_gemm_residual on 4 and a GEMM bias on 2.  A pointer that does not returns
+ *     MES_ERR_ALIGN (the repack and dequantisation helpers need element alignment only).
  *
  * Each entry point names the reference interface (woodx9/minimal-embedding-server, path
  * within that project, file:line) whose computation it replaces.
@@ -206,7 +211,7 @@ int mes_awq_dequant(const int32_t* qweight_mes, const int32_t* qzeros, const voi
  * on tcgen05, bf16 output.  X: bf16 [M, K] (pitch ldx elements); Y: bf16 [M, N] (pitch
  * ldy); bias: bf16 [N] or NULL; scales: f16 [K/G, N]; qzeros: i32 [K/G, N/8].
  * Requirements: N % 128 == 0, K % 128 == 0, group_size == 128, ldx/ldy % 8 == 0,
- * X/Y 16-byte aligned.  M may be any value >= 0. */
+ * X, Y, qweight_mes, qzeros and scales 16-byte aligned.  M may be any value >= 0. */
 int mes_awq_gemm(const void* X, int64_t ldx, const int32_t* qweight_mes,
                  const int32_t* qzeros, const void* scales, const void* bias, void* Y,
                  int64_t ldy, int64_t M, int64_t N, int64_t K, int group_size, void* stream);

@@ -1539,7 +1539,9 @@ int launch_panels(int count, const int32_t* const* qw, const int32_t* const* qze
     if (!qw[i] || !qzeros[i] || !scales[i] || !panels[i]) return MES_ERR_INVALID;
     if (K[i] <= 0 || N[i] <= 0 || K[i] % kGroup || N[i] % 8 || K[i] > (1 << 24) || N[i] > (1 << 24))
       return MES_ERR_INVALID;
-    if (reinterpret_cast<uintptr_t>(panels[i]) & 15) return MES_ERR_ALIGN;
+    if ((reinterpret_cast<uintptr_t>(panels[i]) & 15) || (reinterpret_cast<uintptr_t>(qw[i]) & 3) ||
+        (reinterpret_cast<uintptr_t>(qzeros[i]) & 3) || (reinterpret_cast<uintptr_t>(scales[i]) & 1))
+      return MES_ERR_ALIGN;
     PanelJob& j = jobs.job[i];
     j.qw = (const uint32_t*)qw[i];
     j.qzeros = qzeros[i];
@@ -1658,6 +1660,9 @@ int check_gemm_args(const void* X, int64_t ldx, const int32_t* qw, const int32_t
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+inline bool aligned_to(const void* p, uintptr_t bytes) {
+  return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0;
+}
 
 }  // namespace
 
@@ -1673,6 +1678,7 @@ extern "C" int mes_gemm_take_error(int* code) {
 extern "C" int mes_awq_repack(const int32_t* qweight, int64_t K, int64_t N, int32_t* qweight_mes,
                               void* stream) {
   if (K <= 0 || N <= 0 || K % kGroup || N % 8 || !qweight || !qweight_mes) return MES_ERR_INVALID;
+  if (!aligned_to(qweight, 4) || !aligned_to(qweight_mes, 4)) return MES_ERR_ALIGN;
   const int64_t total = (K / 8) * N;
   int64_t blocks = (total + 255) / 256;
   if (blocks > 65535) blocks = 65535;
@@ -1685,7 +1691,9 @@ extern "C" int mes_awq_dequant(const int32_t* qweight_mes, const int32_t* qzeros
                                int64_t K, int64_t N, int group_size, void* w_out, void* stream) {
   if (K <= 0 || N <= 0 || K % kGroup || N % 8 || group_size != kGroup) return MES_ERR_INVALID;
   if (!qweight_mes || !qzeros || !scales || !w_out) return MES_ERR_INVALID;
-  if (!aligned16(w_out)) return MES_ERR_ALIGN;
+  if (!aligned16(w_out) || !aligned_to(qweight_mes, 4) || !aligned_to(qzeros, 4) ||
+      !aligned_to(scales, 2))
+    return MES_ERR_ALIGN;
   const int64_t total = (K / 8) * N;
   int64_t blocks = (total + 255) / 256;
   if (blocks > 65535) blocks = 65535;
@@ -1715,7 +1723,9 @@ int gemm_entry(int epilogue, const void* X, int64_t ldx, const int32_t* qweight_
                                  epilogue == kEpiSilu ? N / 2 : N);
   if (st != MES_OK) return st < 0 ? MES_OK : st;
   const bool y_ok = epilogue == kEpiResidual ? (reinterpret_cast<uintptr_t>(Y) & 3) == 0 : aligned16(Y);
-  if (!aligned16(X) || !aligned16(qweight_mes) || !y_ok) return MES_ERR_ALIGN;
+  if (!aligned16(X) || !aligned16(qweight_mes) || !aligned16(qzeros) || !aligned16(scales) || !y_ok ||
+      !aligned_to(bias, 2))
+    return MES_ERR_ALIGN;
   if (workspace && !aligned16(workspace)) return MES_ERR_ALIGN;
   if (!workspace) workspace_bytes = 0;
   cudaStream_t s = (cudaStream_t)stream;
@@ -1784,7 +1794,7 @@ extern "C" int mes_awq_gemm_on_panel(int epilogue, const void* X, int64_t ldx, c
   if (M == 0) return MES_OK;
   if (!panel_path(M, N, K) || !X || !panel || !Y) return MES_ERR_INVALID;
   const bool y_ok = epilogue == kEpiResidual ? (reinterpret_cast<uintptr_t>(Y) & 3) == 0 : aligned16(Y);
-  if (!aligned16(X) || !aligned16(panel) || !y_ok) return MES_ERR_ALIGN;
+  if (!aligned16(X) || !aligned16(panel) || !y_ok || !aligned_to(bias, 2)) return MES_ERR_ALIGN;
   cudaStream_t s = (cudaStream_t)stream;
   switch (epilogue) {
     case kEpiBf16:

@@ -368,6 +368,7 @@ inline int grid_for(int64_t work, int threads) {
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+inline bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
 
 }  // namespace
 
@@ -402,7 +403,7 @@ static int launch_embedding(bool f32, const int64_t* ids, int64_t T, const void*
   if (T < 0 || vocab <= 0 || H <= 0 || H % 8) return MES_ERR_INVALID;
   if (T == 0) return MES_OK;
   if (!ids || !table || !out) return MES_ERR_INVALID;
-  if (!aligned16(table) || !aligned16(out)) return MES_ERR_ALIGN;
+  if (!aligned16(table) || !aligned16(out) || !aligned8(ids)) return MES_ERR_ALIGN;
   const int64_t hv = H / 8;
   cudaStream_t s = (cudaStream_t)stream;
   if (f32)
@@ -476,7 +477,8 @@ extern "C" int mes_qknorm_rope(void* qkv, int64_t ld, const int64_t* positions,
   if (T == 0) return MES_OK;
   if (!qkv || !positions || !cos_sin) return MES_ERR_INVALID;
   if (apply_norm && ((Hq > 0 && !q_w) || (Hkv > 0 && !k_w))) return MES_ERR_INVALID;
-  if (!aligned16(qkv) || !aligned16(cos_sin) || (apply_norm && (!aligned16(q_w) || !aligned16(k_w))))
+  if (!aligned16(qkv) || !aligned16(cos_sin) || !aligned8(positions) ||
+      (apply_norm && (!aligned16(q_w) || !aligned16(k_w))))
     return MES_ERR_ALIGN;
   const int64_t units = T * (((int64_t)Hq + Hkv + kGroupHeads - 1) / kGroupHeads);
   if (units > 0x7fffffffLL - 256) return MES_ERR_INVALID;
@@ -516,7 +518,7 @@ extern "C" int mes_last_token_l2(const void* hidden, int64_t T, int64_t H, const
   if (T < 0 || H <= 0 || H % 8 || B < 0) return MES_ERR_INVALID;
   if (B == 0) return MES_OK;
   if (!hidden || !idx || !out || T == 0) return MES_ERR_INVALID;
-  if (!aligned16(hidden) || !aligned16(out)) return MES_ERR_ALIGN;
+  if (!aligned16(hidden) || !aligned16(out) || !aligned8(idx)) return MES_ERR_ALIGN;
   const int hv = (int)(H / 8);
   const int threads = hv >= 256 ? 256 : ((hv + 31) / 32) * 32;
   last_token_l2_kernel<<<(unsigned)B, threads, 0, (cudaStream_t)stream>>>(
@@ -532,7 +534,7 @@ extern "C" int64_t mes_varlen_workspace_size(int64_t T) {
 extern "C" int mes_varlen_schedule(const int64_t* positions, int64_t T, void* workspace,
                                    void* stream) {
   if (T <= 0 || T > 0x3fffffffLL || !positions || !workspace) return MES_ERR_INVALID;
-  if (reinterpret_cast<uintptr_t>(workspace) & 255) return MES_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) || !aligned8(positions)) return MES_ERR_ALIGN;
   char* ws = static_cast<char*>(workspace);
   varlen_schedule_kernel<<<1, kSchedThreads, 0, (cudaStream_t)stream>>>(
       positions, (int)T, (int*)ws, (int*)(ws + cu_offset()), (int2*)(ws + items_offset(T)));

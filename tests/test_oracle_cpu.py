@@ -1,5 +1,6 @@
 """CPU tests: the oracle against the reference's golden fixtures, the AWQ format against
 vLLM's packer, and the C-ABI library's exports (no GPU work)."""
+import ctypes
 import os
 import re
 
@@ -193,6 +194,25 @@ def test_host_argument_checks_reject_without_gpu_work():
     assert lib.mes_awq_panels(0, None, None, None, None, None, None, None) == 1
     assert lib.mes_wait_probe(0, 0, None) == 1             # limit out of range
     assert lib.mes_wait_probe(1_000_000_000, 0, None) == 1
+    # Pointers that do not start on the boundary their elements (or TMA) need are refused
+    # with MES_ERR_ALIGN before anything is launched (the addresses are never dereferenced).
+    a, odd4, odd2 = 0x10000, 0x10004, 0x10002
+    assert lib.mes_embedding(odd4, 4, a, 10, 8, a, None) == 2                  # ids (i64)
+    assert lib.mes_embedding_f32(odd4, 4, a, 10, 8, a, None) == 2
+    assert lib.mes_qknorm_rope(a, 256, odd4, a, 1, 64, None, None, 4, 1, 1, 128, 1e-6, 0,
+                               None) == 2                                         # positions
+    assert lib.mes_last_token_l2(a, 4, 8, odd4, 1, a, None) == 2                 # indices
+    assert lib.mes_varlen_schedule(odd4, 4, a, None) == 2                         # positions
+    assert lib.mes_awq_repack(odd2, 128, 8, a, None) == 2                         # i32 words
+    assert lib.mes_awq_dequant(a, odd2, a, 128, 8, 128, a, None) == 2
+    assert lib.mes_awq_dequant(a, a, a + 1, 128, 8, 128, a, None) == 2           # f16 scales
+    vp = ctypes.c_void_p
+    i64 = ctypes.c_int64
+    assert lib.mes_awq_panels(1, (vp * 1)(a), (vp * 1)(odd2), (vp * 1)(a), (i64 * 1)(128),
+                              (i64 * 1)(8), (vp * 1)(a), None) == 2
+    for qz, sc, b in ((odd4, a, None), (a, odd4, None), (a, a, a + 1)):         # TMA-read / bias
+        assert lib.mes_awq_gemm(a, 128, a, qz, sc, b, a, 128, 16, 128, 128, 128, None) == 2
+    assert lib.mes_awq_gemm_on_panel(0, a, 1024, a, a + 1, a, 1024, 2048, 1024, 1024, None) == 2
 
 
 def test_cpu_tensors_raise_instead_of_falling_back():
